@@ -1,0 +1,470 @@
+"""Benchmark of the fused 3S hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c4] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+A step is one fused forward (SDDMM + online softmax + SpMM) over every row
+window of the graph, all heads, inputs resident in HBM.  Metric: GEdges*heads/s
+= E * H / t_step (E = CSR nnz).  The graph is converted and ordered once
+before timing (it is static across steps, as in a GNN layer); the converter
+and order times are reported beside the metric.
+
+With N > 1 GPUs the row windows are sharded (contiguous, cost-balanced),
+K / V replicated, the fixed graph split across ranks (strong scaling); the
+step time is the max over ranks of device time.
+
+--impl reference times the reference's own CPU implementation
+(cpu_block_sparse_attention, tests/test_fused_3s_v2.cu:17, compiled from its
+sources into oracle/_ref) with all host threads on a bounded, seeded sample of
+windows per step, extrapolated to the full step by block count.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "GEdges*heads/s"
+UNIT = "GEdges*heads/s"
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def ncu_traffic(config: str):
+    """DRAM bytes per fused launch from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / f"fused3s_{config}_ncu.md"
+    if not p.exists():
+        return None
+    m = re.search(r"dram_bytes_per_launch_full:\s*([0-9.eE+]+)", p.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.proc = None
+        self.gpu_id = gpu_id
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", self.gpu_id], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------
+# workload
+# ----------------------------------------------------------------------------
+
+def build_workload(config: str, device):
+    import torch
+    from fused3s_b200 import graphs as G
+    cfg = G.CONFIGS[config]
+    t0 = time.time()
+    g = G.make_graph(config, device=str(device) if config in ("c4", "c5") else "cpu")
+    log(f"[bench] graph {config}: N={g.num_nodes} E={g.num_edges} ({time.time() - t0:.1f}s)")
+    return g, cfg
+
+
+def make_features_device(n, h, d, kind, seed, device):
+    """fp16 [n, h, d] Q, K, V generated on the device in row chunks."""
+    import torch
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    out = []
+    chunk = max(1, (1 << 27) // (h * d))
+    for _ in range(3):
+        t = torch.empty((n, h, d), dtype=torch.float16, device=device)
+        for r in range(0, n, chunk):
+            rr = min(n, r + chunk)
+            if kind == "uniform":
+                x = torch.rand((rr - r, h, d), generator=gen, device=device) * 2 - 1
+            else:
+                x = torch.randn((rr - r, h, d), generator=gen, device=device) / math.sqrt(d)
+            t[r:rr] = x.to(torch.float16)
+        out.append(t)
+    return out
+
+
+def alg_bytes(heads, d, B, nrw):
+    """Algorithmic HBM bytes of one forward: per head, K and V tiles of every
+    active block (64*d B), the Q tile (32*d B) and fp32 O tile (64*d B) of
+    every window; plus the block-column list and window offsets."""
+    return heads * (64 * d * B + 96 * d * nrw) + 4 * B + 8 * nrw
+
+
+def alg_flops(heads, d, B):
+    return 1024 * d * heads * B
+
+
+# ----------------------------------------------------------------------------
+# CPU baseline (reference's own cpu_block_sparse_attention, or the port)
+# ----------------------------------------------------------------------------
+
+def cpu_sample_run(g, off, cols, q, k, v, budget_s, seed, threads):
+    """Run the reference CPU function on a seeded random sample of windows,
+    head 0, sized to ~budget_s seconds; returns (seconds, sampled blocks,
+    windows, kind)."""
+    import oracle
+    kind = "reference" if oracle.ref_available() else "port"
+    cnt = np.diff(off)
+    rng = np.random.default_rng(seed)
+    perm = rng.permutation(len(cnt))
+    nonempty = perm[cnt[perm] > 0]
+
+    def run(wins):
+        t = time.perf_counter()
+        if kind == "reference":
+            oracle.ref_block_attention(g.num_nodes, q, k, v, off, cols, windows=wins, threads=threads)
+        else:
+            oracle.block_attention(g.num_nodes, q, k, v, off, cols, windows=wins, threads=threads)
+        return time.perf_counter() - t
+
+    # calibrate on a small sample, then size the real one
+    n0 = min(len(nonempty), max(threads * 4, 64))
+    w0 = np.sort(nonempty[:n0]).astype(np.int32)
+    t0 = run(w0)
+    per_block = max(t0, 1e-4) / max(int(cnt[w0].sum()), 1)
+    want_blocks = budget_s / per_block
+    csum = np.cumsum(cnt[nonempty])
+    n1 = int(min(len(nonempty), max(n0, np.searchsorted(csum, want_blocks) + 1)))
+    w1 = np.sort(nonempty[:n1]).astype(np.int32)
+    t1 = run(w1)
+    return t1, int(cnt[w1].sum()), n1, kind
+
+
+def head0_f32(t):
+    return t[:, 0, :].float().contiguous().cpu().numpy()
+
+
+# ----------------------------------------------------------------------------
+# arms
+# ----------------------------------------------------------------------------
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    import torch
+    from fused3s_b200 import graphs as G
+    import oracle
+    config = args.config
+    cfg = G.CONFIGS[config]
+    g = G.make_graph(config, device="cuda" if (config in ("c4", "c5") and torch.cuda.is_available()) else "cpu")
+    conv = oracle.ref_convert if oracle.ref_available() else oracle.convert
+    off, cols = conv(g.num_nodes, g.row_ptr, g.col_ind)
+    B, nrw = int(cols.shape[0]), len(off) - 1
+    q, k, v = G.make_features(g.num_nodes, 1, cfg.head_dim, kind=cfg.features, seed=42)
+    q, k, v = (x[:, 0, :].float().numpy() for x in (q, k, v))
+    threads = os.cpu_count() or 1
+    total_s, samples = 0.0, []
+    for step in range(args.warmup + args.steps):
+        t, blocks, nw, kind = cpu_sample_run(g, off, cols, q, k, v, args.ref_step_budget, seed=step, threads=threads)
+        full_s = t * (B * cfg.heads) / max(blocks, 1)
+        if step >= args.warmup:
+            samples.append(full_s)
+    full_s = statistics.median(samples)
+    value = g.num_edges * cfg.heads / full_s / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": full_s * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": config, "description": cfg.description, "num_nodes": g.num_nodes,
+                   "num_edges": g.num_edges, "heads": cfg.heads, "head_dim": cfg.head_dim, "blocks": B,
+                   "row_windows": nrw},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"per step: seeded random windows of head 0 sized to ~{args.ref_step_budget:.0f}s "
+                                   f"of CPU work ({blocks} of {B} blocks), time extrapolated by block count "
+                                   f"to all {B} blocks x {cfg.heads} heads"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import fused3s_b200 as F
+    from fused3s_b200 import _lib, shard
+
+    rank, world, local = dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lib = _lib.load()
+    g, cfg = build_workload(args.config, dev)
+    H, d = cfg.heads, cfg.head_dim
+    N, E = g.num_nodes, g.num_edges
+
+    # format: converted and ordered once (timed separately, not part of the step)
+    rp = torch.from_numpy(g.row_ptr).to(dev)
+    ci = torch.from_numpy(g.col_ind).to(dev)
+    F.convert_csr_to_block_sparse(N, rp, ci)  # warm the converter
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    fmt = F.convert_csr_to_block_sparse(N, rp, ci)
+    convert_ms = (time.perf_counter() - t0) * 1e3
+    t0 = time.perf_counter()
+    order = F.generate_balanced_window_order(fmt)
+    torch.cuda.synchronize()
+    order_ms = (time.perf_counter() - t0) * 1e3
+    del rp, ci
+    B, nrw = fmt.num_blocks, fmt.num_row_windows
+    off_h = fmt.window_offsets.cpu().numpy()
+
+    parts = shard.partition_windows(off_h, world)
+    lo, hi = parts[rank]
+    r0, r1 = shard.slab_rows(lo, hi, N)
+    my_order = shard.rank_order(order, lo, hi).contiguous()
+    Qf, Kf, Vf = make_features_device(N, H, d, cfg.features, 42, dev)
+    Q = Qf[r0:r1].contiguous()
+    del Qf
+    O = torch.empty((r1 - r0, H, d), dtype=torch.float32, device=dev)
+    ws = F.forward_workspace(dev)
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+    n_items = int(my_order.numel())
+
+    def step():
+        st = lib.f3s_forward(Q.data_ptr(), Kf.data_ptr(), Vf.data_ptr(), O.data_ptr(),
+                             fmt.window_offsets.data_ptr(), fmt.block_col_indices.data_ptr(),
+                             my_order.data_ptr(), n_items, N, H, d, lo, r1 - r0, ws.data_ptr(), ws.numel(), sptr)
+        if st != 0:
+            raise _lib.Fused3SError(st, "f3s_forward")
+
+    for _ in range(args.warmup):
+        step()
+    st = lib.f3s_workspace_status(ws.data_ptr(), sptr)
+    if st != 0:
+        raise _lib.Fused3SError(st, "f3s_forward (device, warm-up)")
+
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        uuid = str(dev.index)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(uuid) as clk:
+        evs[0].record(stream)
+        for i in range(args.steps):
+            step()
+            evs[i + 1].record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    per_step = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    total_ms = evs[0].elapsed_time(evs[-1])
+    st = lib.f3s_workspace_status(ws.data_ptr(), sptr)
+    if st != 0:
+        raise _lib.Fused3SError(st, "f3s_forward (device, timed)")
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    value = E * H / (ms_per_step / 1e3) / 1e9
+
+    # end to end through the public API: pinned host Q/K/V -> device, forward,
+    # O -> pinned host, every step
+    e2e = None
+    h2d = (Q.numel() + Kf.numel() + Vf.numel()) * 2
+    d2h = O.numel() * 4
+    if not args.no_e2e and h2d + d2h < 8e9:
+        hQ = Q.cpu().pin_memory()
+        hK = Kf.cpu().pin_memory()
+        hV = Vf.cpu().pin_memory()
+        hO = torch.empty(O.shape, dtype=torch.float32).pin_memory()
+        dQ, dK, dV = torch.empty_like(Q), torch.empty_like(Kf), torch.empty_like(Vf)
+
+        def e2e_step():
+            dQ.copy_(hQ, non_blocking=True)
+            dK.copy_(hK, non_blocking=True)
+            dV.copy_(hV, non_blocking=True)
+            F.fused3s_forward(dQ, dK, dV, fmt, order=my_order, out=O, q_window_base=lo)
+            hO.copy_(O, non_blocking=True)
+
+        for _ in range(max(1, args.warmup // 2)):
+            e2e_step()
+        ee = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ee[0].record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        ee[1].record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = ee[0].elapsed_time(ee[1])
+        if world > 1:
+            t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e_step_ms = e2e_ms / args.steps
+        e2e = {"value": E * H / (e2e_step_ms / 1e3) / 1e9, "unit": UNIT, "ms_per_step": e2e_step_ms,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "note": "per rank: pinned host Q slab + K + V -> device, fused forward, O slab -> host"}
+        del hQ, hK, hV, hO, dQ, dK, dV
+
+    # optional all-gather of O (only when the full output is needed on every rank)
+    gather_ms = None
+    if world > 1 and args.gather:
+        slabs = [shard.slab_rows(a, b, N) for a, b in parts]
+        ge = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        shard.gather_rows(O, slabs)
+        dist.barrier()
+        torch.cuda.synchronize()
+        ge[0].record(stream)
+        full_o = shard.gather_rows(O, slabs)
+        ge[1].record(stream)
+        torch.cuda.synchronize()
+        gather_ms = ge[0].elapsed_time(ge[1])
+        del full_o
+
+    # roofline of the fused kernel (per launch, this rank's share)
+    my_blocks = int((off_h[1:] - off_h[:-1])[lo:hi].sum())
+    my_windows = hi - lo
+    kern_ms = statistics.median(per_step)
+    bytes_launch = alg_bytes(H, d, my_blocks, my_windows)
+    flops_launch = alg_flops(H, d, my_blocks)
+    hbm_peak, tc_peak, peak_kind = measured_peaks()
+    achieved = bytes_launch / (kern_ms / 1e3) / 1e9
+    traffic = ncu_traffic(args.config) if world == 1 else None
+
+    result = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            off_np, cols_np = fmt.to_host()
+            q0, k0, v0 = head0_f32(Q), head0_f32(Kf), head0_f32(Vf)
+            t, blocks, nw, kind = cpu_sample_run(g, off_np, cols_np, q0, k0, v0, args.cpu_budget, 0, threads)
+            full_s = t * (B * H) / max(blocks, 1)
+            cpu = {"value": E * H / full_s / 1e9, "unit": UNIT, "cores": threads, "kind": kind,
+                   "sample": f"{nw} seeded random windows of head 0 ({blocks} of {B} blocks, {t:.1f}s on "
+                             f"{threads} threads), extrapolated by block count to {B} blocks x {H} heads"}
+        clocks = clk.summary()
+        result = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 in / f32 accumulate", "data": "synthetic",
+            "config": {"workload": args.config, "description": cfg.description, "num_nodes": N, "num_edges": E,
+                       "heads": H, "head_dim": d, "blocks": B, "row_windows": nrw,
+                       "parallelism": f"row-window shards x{world}, K/V replicated",
+                       "l2": "inputs larger than L2" if (Kf.numel() + Vf.numel()) * 2 > 126e6 else
+                             "inputs fit in L2 (no flush)",
+                       "convert_ms": convert_ms, "order_ms": order_ms},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "traffic": traffic, "peak_kind": peak_kind,
+                         "alg_bytes_per_launch": bytes_launch, "kernel_ms": kern_ms,
+                         "tensor_tflops": flops_launch / (kern_ms / 1e3) / 1e12, "tensor_peak": tc_peak,
+                         "tensor_frac": flops_launch / (kern_ms / 1e3) / 1e12 / tc_peak},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+        }
+        if gather_ms is not None:
+            result["allgather_o_ms"] = gather_ms
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c4", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--gather", action="store_true", help="also time the NCCL all-gather of O (N > 1)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU work for cpu_baseline")
+    ap.add_argument("--ref-step-budget", type=float, default=3.0, help="seconds of CPU work per reference step")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

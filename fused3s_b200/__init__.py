@@ -1,0 +1,34 @@
+"""fused3s_b200 -- a B200-native (sm_100a) fused 3S engine.
+
+CSR -> 16x16 block-sparse row windows -> descending-workload window order ->
+fused SDDMM + online softmax + SpMM -> fp32 O, all on the GPU, behind the
+C ABI of libfused3s.so (include/fused3s.h) and the reference-shaped host API
+below.
+"""
+from .api import (
+    BlockSparseFormat,
+    GraphData,
+    Fused3SError,
+    convert_csr_to_block_sparse,
+    f3s_1tb1rw_kernel,
+    float2half,
+    forward_workspace,
+    fused3s_forward,
+    generate_balanced_window_order,
+    load_csr_graph,
+    workspace_status,
+)
+
+__all__ = [
+    "BlockSparseFormat",
+    "GraphData",
+    "Fused3SError",
+    "convert_csr_to_block_sparse",
+    "f3s_1tb1rw_kernel",
+    "float2half",
+    "forward_workspace",
+    "fused3s_forward",
+    "generate_balanced_window_order",
+    "load_csr_graph",
+    "workspace_status",
+]

@@ -1,0 +1,274 @@
+"""Python host API of the B200 fused 3S engine.
+
+It mirrors the reference's host interface for the fused3s_v2 path, with the
+same names and argument meanings, computed on the GPU through the C ABI of
+libfused3s.so (include/fused3s.h):
+
+  GraphData, load_csr_graph            include/utils.cuh:19-40
+  BlockSparseFormat                    include/utils.cuh:42-46 (blockSparseFormat)
+  convert_csr_to_block_sparse          src/converter.cu:13-44
+  generate_balanced_window_order       include/utils.cuh:48-59
+  f3s_1tb1rw_kernel                    src/fused3s_v2.cu:81-90 (same argument list)
+  float2half                           tests/test_fused_3s_v2.cu:61-64
+
+plus the extended forward `fused3s_forward` (true num_nodes with masking of
+columns >= N, H heads, head_dim 64/128, window subsets for sharding).
+
+Differences from the reference, each deliberate:
+  * errors raise Fused3SError instead of exit() (CUDA_CHECK, utils.cuh:9-17);
+  * load_csr_graph reads col_idx.txt, the name data/data_loader.py writes
+    (the reference opens col_ind.txt and silently reads zeros, utils.cuh:36);
+  * the window order breaks ties by ascending window id (stable); the block
+    count sequence along the order equals the reference's std::sort result.
+"""
+from __future__ import annotations
+
+import dataclasses
+import os
+from typing import Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import Fused3SError, check
+
+
+# ----------------------------------------------------------------------------
+# containers
+# ----------------------------------------------------------------------------
+
+@dataclasses.dataclass
+class GraphData:
+    """CSR graph (include/utils.cuh:19-24)."""
+    num_nodes: int
+    num_edges: int
+    row_ptr: np.ndarray  # int32 [num_nodes + 1]
+    col_ind: np.ndarray  # int32 [num_edges]
+
+
+@dataclasses.dataclass
+class BlockSparseFormat:
+    """16x16 block-sparse row windows (include/utils.cuh:42-46), device-resident."""
+    num_row_windows: int
+    window_offsets: torch.Tensor     # int32 [nrw + 1] on the GPU
+    block_col_indices: torch.Tensor  # int32 [B] on the GPU
+    num_nodes: int
+
+    @property
+    def num_blocks(self) -> int:
+        return int(self.block_col_indices.shape[0])
+
+    def to_host(self):
+        return (self.window_offsets.cpu().numpy(), self.block_col_indices.cpu().numpy())
+
+
+def load_csr_graph(dataset_dir: str) -> GraphData:
+    """Read meta.txt / row_ptr.txt / col_idx.txt written by the reference's
+    data/data_loader.py (include/utils.cuh:26-40, with the column file name
+    fixed; col_ind.txt is accepted too)."""
+    with open(os.path.join(dataset_dir, "meta.txt")) as f:
+        num_nodes, num_edges = (int(x) for x in f.read().split()[:2])
+    row_ptr = np.loadtxt(os.path.join(dataset_dir, "row_ptr.txt"), dtype=np.int64).reshape(-1)
+    col_path = os.path.join(dataset_dir, "col_idx.txt")
+    if not os.path.exists(col_path):
+        col_path = os.path.join(dataset_dir, "col_ind.txt")
+    col_ind = np.loadtxt(col_path, dtype=np.int64).reshape(-1)
+    if row_ptr.shape[0] != num_nodes + 1 or col_ind.shape[0] != num_edges:
+        raise ValueError(f"{dataset_dir}: sizes disagree with meta.txt")
+    return GraphData(num_nodes, num_edges, row_ptr.astype(np.int32), col_ind.astype(np.int32))
+
+
+# ----------------------------------------------------------------------------
+# helpers
+# ----------------------------------------------------------------------------
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+class _WorkspaceCache:
+    """Grow-only device workspaces, one per (device, stream, purpose)."""
+
+    def __init__(self):
+        self._ws = {}
+
+    def get(self, device: torch.device, kind: str, nbytes: int) -> torch.Tensor:
+        key = (device.index, _stream_ptr(device), kind)
+        ws = self._ws.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+            self._ws[key] = ws
+        return ws
+
+
+_WS = _WorkspaceCache()
+
+
+def _as_device_i32(x, device: torch.device) -> torch.Tensor:
+    if isinstance(x, torch.Tensor):
+        return x.to(device=device, dtype=torch.int32).contiguous()
+    return torch.from_numpy(np.ascontiguousarray(np.asarray(x, dtype=np.int32))).to(device)
+
+
+def _default_device(device) -> torch.device:
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    device = torch.device(device)
+    if device.type != "cuda":
+        raise ValueError("fused3s_b200 runs on CUDA devices only (no CPU fallback)")
+    return device
+
+
+# ----------------------------------------------------------------------------
+# converter / order
+# ----------------------------------------------------------------------------
+
+def convert_csr_to_block_sparse(num_nodes: int, row_ptr, col_ind, device=None) -> BlockSparseFormat:
+    """CSR -> block-sparse row windows on the GPU (src/converter.cu:13-44).
+
+    Bit-exact to the reference converter.  Raises Fused3SError with
+    F3S_ERR_BAD_CSR on a column outside [0, N) or a decreasing row_ptr.
+    Synchronises (returns exact-size arrays)."""
+    lib = _lib.load()
+    device = _default_device(device)
+    rp = _as_device_i32(row_ptr, device)
+    ci = _as_device_i32(col_ind, device)
+    nnz = int(ci.numel())
+    if rp.numel() != num_nodes + 1:
+        raise ValueError("row_ptr must have num_nodes + 1 entries")
+    nrw = (num_nodes + 15) // 16
+    offsets = torch.empty(nrw + 1, dtype=torch.int32, device=device)
+    cols = torch.empty(max(nnz, 1), dtype=torch.int32, device=device)
+    wsz = lib.f3s_convert_workspace_size(num_nodes, nnz)
+    ws = _WS.get(device, "convert", wsz)
+    nb = _lib._I64(0)
+    with torch.cuda.device(device):
+        st = lib.f3s_convert(_ptr(rp), _ptr(ci) if nnz else None, num_nodes, nnz, _ptr(offsets),
+                             _ptr(cols), _ptr(ws), ws.numel(), nb, _stream_ptr(device))
+    check(st, "f3s_convert")
+    return BlockSparseFormat(nrw, offsets, cols[: nb.value], num_nodes)
+
+
+def generate_balanced_window_order(fmt: BlockSparseFormat) -> torch.Tensor:
+    """Window ids sorted by active-block count, descending (include/utils.cuh:48-59)."""
+    lib = _lib.load()
+    device = fmt.window_offsets.device
+    order = torch.empty(max(fmt.num_row_windows, 1), dtype=torch.int32, device=device)
+    ws = _WS.get(device, "order", lib.f3s_window_order_workspace_size(fmt.num_row_windows))
+    with torch.cuda.device(device):
+        st = lib.f3s_window_order(_ptr(fmt.window_offsets), fmt.num_row_windows, _ptr(order), _ptr(ws),
+                                  ws.numel(), _stream_ptr(device))
+    check(st, "f3s_window_order")
+    return order[: fmt.num_row_windows]
+
+
+# ----------------------------------------------------------------------------
+# fused forward
+# ----------------------------------------------------------------------------
+
+def _check_features(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor):
+    for name, t in (("Q", Q), ("K", K), ("V", V)):
+        if t.dtype != torch.float16:
+            raise TypeError(f"{name} must be float16")
+        if t.device.type != "cuda":
+            raise ValueError(f"{name} must be on a CUDA device")
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    if K.shape != V.shape:
+        raise ValueError("K and V must have the same shape")
+
+
+def _as_nhd(t: torch.Tensor) -> torch.Tensor:
+    return t.unsqueeze(1) if t.dim() == 2 else t
+
+
+def fused3s_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: BlockSparseFormat,
+                    order: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                    q_window_base: int = 0, check_status: bool = False) -> torch.Tensor:
+    """O = block-sparse softmax(Q K^T) V, fused (the fused3s_v2 path).
+
+    Q: fp16 [q_rows, H, d] (or [q_rows, d] for one head) holding rows
+       16*q_window_base ... of the full Q;  K, V: fp16 [N, H, d] (or [N, d]).
+    order: int32 window ids to compute (default: every window of the slab in
+       the balanced order).  Returns fp32 O shaped like Q; rows of the listed
+       windows are written in full (zeros for windows with no block).
+    check_status: synchronise and raise if a kernel recorded an error."""
+    lib = _lib.load()
+    _check_features(Q, K, V)
+    q3, k3 = _as_nhd(Q), _as_nhd(K)
+    q_rows, heads, head_dim = q3.shape
+    num_nodes = k3.shape[0]
+    if k3.shape[1:] != (heads, head_dim):
+        raise ValueError("Q, K, V must agree on heads and head_dim")
+    if num_nodes != fmt.num_nodes:
+        raise ValueError("K/V rows must equal the graph's num_nodes")
+    device = Q.device
+    if order is None:
+        if q_window_base == 0 and q_rows == num_nodes:
+            order = generate_balanced_window_order(fmt)
+        else:
+            order = torch.arange(q_window_base, q_window_base + (q_rows + 15) // 16, dtype=torch.int32,
+                                 device=device)
+    order = order.to(device=device, dtype=torch.int32).contiguous()
+    if out is None:
+        out = torch.empty(Q.shape, dtype=torch.float32, device=device)
+    elif out.dtype != torch.float32 or out.shape != Q.shape or not out.is_contiguous():
+        raise ValueError("out must be a contiguous float32 tensor shaped like Q")
+    ws = _WS.get(device, "forward", lib.f3s_forward_workspace_size())
+    with torch.cuda.device(device):
+        st = lib.f3s_forward(_ptr(Q), _ptr(K), _ptr(V), _ptr(out), _ptr(fmt.window_offsets),
+                             _ptr(fmt.block_col_indices), _ptr(order), int(order.numel()), num_nodes, heads,
+                             head_dim, q_window_base, q_rows, _ptr(ws), ws.numel(), _stream_ptr(device))
+        check(st, "f3s_forward")
+        if check_status:
+            check(lib.f3s_workspace_status(_ptr(ws), _stream_ptr(device)), "f3s_forward (device)")
+    return out
+
+
+def forward_workspace(device=None) -> torch.Tensor:
+    """The workspace fused3s_forward uses on the current stream of `device`."""
+    device = _default_device(device)
+    return _WS.get(device, "forward", _lib.load().f3s_forward_workspace_size())
+
+
+def workspace_status(ws: torch.Tensor) -> int:
+    """Synchronise and return (and clear) the first error a kernel recorded in ws."""
+    return _lib.load().f3s_workspace_status(_ptr(ws), _stream_ptr(ws.device))
+
+
+def f3s_1tb1rw_kernel(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, O_out: torch.Tensor,
+                      window_offsets: torch.Tensor, block_col_indices: torch.Tensor,
+                      window_order: torch.Tensor, num_row_windows: int, feat_dim: int) -> None:
+    """Drop-in for the reference kernel launch <<<nrw, dim3(32,4)>>> (src/fused3s_v2.cu:81-90):
+    same arguments, buffers with num_row_windows*16 rows, every row treated as
+    a node (no masking of padded columns, like the reference v2 kernel)."""
+    lib = _lib.load()
+    rows = num_row_windows * 16
+    for name, t, dt in (("Q", Q, torch.float16), ("K", K, torch.float16), ("V", V, torch.float16),
+                        ("O_out", O_out, torch.float32)):
+        if t.dtype != dt or not t.is_contiguous() or t.numel() < rows * feat_dim:
+            raise ValueError(f"{name}: expected contiguous {dt} with {rows}x{feat_dim} elements")
+    device = Q.device
+    with torch.cuda.device(device):
+        st = lib.f3s_1tb1rw_launch(_ptr(Q), _ptr(K), _ptr(V), _ptr(O_out), _ptr(window_offsets),
+                                   _ptr(block_col_indices), _ptr(window_order), num_row_windows, feat_dim,
+                                   _stream_ptr(device))
+    check(st, "f3s_1tb1rw_launch")
+
+
+def float2half(x: torch.Tensor) -> torch.Tensor:
+    """fp32 -> fp16 round-to-nearest on the GPU (tests/test_fused_3s_v2.cu:61-64)."""
+    lib = _lib.load()
+    if x.dtype != torch.float32 or x.device.type != "cuda":
+        raise TypeError("float2half expects a CUDA float32 tensor")
+    x = x.contiguous()
+    out = torch.empty(x.shape, dtype=torch.float16, device=x.device)
+    with torch.cuda.device(x.device):
+        st = lib.f3s_half_from_float(_ptr(x), _ptr(out), x.numel(), _stream_ptr(x.device))
+    check(st, "f3s_half_from_float")
+    return out

@@ -1,0 +1,607 @@
+// f3s_forward.cu -- fused SDDMM + online softmax + SpMM over 16x16 block-sparse
+// row windows, for sm_100a.
+//
+// Semantics: tests/test_fused_3s_v2.cu:17-59 (block semantics: every column
+// of every active block of the row's window is scored; columns >= N are
+// masked), computed the way src/fused3s_v2.cu:81-246 does (fp16 Q/K/V, fp32
+// scores, online softmax with fp32 running max / sum, P rounded to fp16 for
+// P.V, fp32 accumulation, fp32 O).
+//
+// Design (B200-first, not a translation of the v2 kernel):
+//   * Persistent CTAs, one per SM, pull work items (window, head-group) from a
+//     device-wide ticket counter in the caller's workspace, in the order given
+//     by `order` (descending workload), so heavy windows start first and the
+//     tail balances itself.
+//   * Memory layout is node-major [N, H, d] fp16.  A CTA takes HG heads of a
+//     window at once, so one active block's K (or V) tile is 16 * HG * d * 2
+//     contiguous bytes in HBM: a single TMA bulk-tensor load per tile
+//     (3-D tensor map {64 elems, node, head-chunk}, 128-byte swizzle) lands it
+//     in shared memory as [head-chunk][16 nodes][64 elems] rows of 128 B,
+//     ready for conflict-free ldmatrix.
+//   * Warp specialisation: warp 8 is the producer (ticket fetch, window
+//     metadata, block-column list read 32 at a time, TMA issue into a ring of
+//     STAGES K/V stages guarded by full/empty mbarriers); warps 0-7 consume.
+//     Consumer warp (hh, sp) owns head hh of the group and every SPLITS-th
+//     block of the window (SPLITS = 8 / HG); partial (m, l, O) of the splits
+//     are merged through shared memory at the end of the window.
+//   * Per block and head: S = Q K^T with mma.sync m16n8k16 (Q fragments stay
+//     in registers for the whole window), row max / sum with quad shuffles,
+//     exp2 on the MUFU, P packed to fp16 straight from the accumulator
+//     fragments into the A operand of O += P V (V via ldmatrix.trans).
+//     16-wide contractions are too narrow for tcgen05's M >= 64 tiles without
+//     packing unrelated windows; at 16 flop/byte the kernel is HBM-bound and
+//     the warp-level tensor path is not the limiter.
+//   * Every mbarrier wait is bounded (global timer) and aborts the CTA with a
+//     status word in the workspace instead of hanging.
+#include <algorithm>
+#include <mutex>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include "f3s_internal.cuh"
+
+namespace f3s {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kFwdThreads = (kConsumerWarps + 1) * 32;
+constexpr int kSmemBudget = 227 * 1024;
+constexpr uint64_t kWaitTimeoutNs = 10ull * 1000 * 1000 * 1000;  // 10 s: far above any legal wait
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int D, int HG>
+struct FwdCfg {
+    static constexpr int SPLITS = kConsumerWarps / HG;
+    static constexpr int HC = HG * D / 64;           // 128-byte rows per node in one tile
+    static constexpr int TILE = 16 * HG * D * 2;     // bytes of one Q, K or V tile
+    static constexpr int SLOT_F = 16 * D + 64;       // floats per merge slot (O partial + m/l)
+    static constexpr int MERGE = (SPLITS - 1) * HG * SLOT_F * 4;
+    // Q double buffer + merge area + barriers/metadata (<= 1 KB for <= 32
+    // stages) + 1 KB slack for aligning the dynamic shared memory base
+    static constexpr int FIXED = 2 * TILE + MERGE + 1024 + 1024;
+    static constexpr int STAGES_FIT = (kSmemBudget - FIXED) / (2 * TILE);
+    static constexpr int STAGES = STAGES_FIT > 32 ? 32 : STAGES_FIT;
+    static constexpr int Q_OFF = 0;
+    static constexpr int KV_OFF = 2 * TILE;
+    static constexpr int MERGE_OFF = KV_OFF + STAGES * 2 * TILE;
+    static constexpr int BAR_OFF = MERGE_OFF + MERGE;
+    static constexpr int NBARS = 2 * STAGES + 6;
+    static constexpr int META_OFF = BAR_OFF + NBARS * 8;
+    static constexpr int WINFO_OFF = (META_OFF + STAGES * 4 + 15) / 16 * 16;
+    static constexpr int SMEM = WINFO_OFF + 2 * 16 + 1024;  // + slack to align the base to 1 KB
+    static_assert(STAGES >= 2, "need at least two K/V stages");
+    static_assert(SMEM <= kSmemBudget, "shared memory budget");
+    static_assert(D % 64 == 0, "head_dim must be a multiple of 64");
+};
+
+struct FwdParams {
+    float* O;
+    const int* offsets;
+    const int* cols;
+    const int* order;
+    WsHeader* hdr;
+    uint64_t timeout_ns;
+    int num_items;      // entries of `order`
+    int groups;         // head groups per window (heads / HG)
+    int num_nodes;      // N (rows of K and V)
+    int nrw_total;      // ceil(N / 16)
+    int heads;          // H
+    int q_window_base;  // first window of the Q / O slab
+    int q_windows;      // windows in the slab
+    int q_rows;         // rows of the Q / O slab
+    int tail;           // N % 16 (0: no masked column)
+    int tma3d;          // 1: one 3-D TMA load per tile; 0: HC 2-D loads
+};
+
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, const ErrorSink& e, uint64_t tmo) {
+    bool ok = mbar_wait_bounded(bar, parity, e, tmo);
+    return __all_sync(0xffffffffu, ok);
+}
+
+template <int HC>
+__device__ __forceinline__ void load_tile(const CUtensorMap* tm, uint32_t dst, uint32_t bar, int row, int z0,
+                                          int tma3d) {
+    if (tma3d) {
+        tma_load_3d(dst, tm, bar, 0, row, z0);
+    } else {
+#pragma unroll
+        for (int j = 0; j < HC; ++j) tma_load_2d(dst + j * 2048, tm, bar, (z0 + j) * 64, row);
+    }
+}
+
+template <int D, int HG>
+__global__ void __launch_bounds__(kFwdThreads, 1)
+    k_fused3s(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+              const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
+    using C = FwdCfg<D, HG>;
+    constexpr int S = C::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_addr(smem_raw);
+    const uint32_t sbase = (raw + 1023u) & ~1023u;
+    uint8_t* sp8 = smem_raw + (sbase - raw);
+    const uint32_t q_s = sbase + C::Q_OFF;
+    const uint32_t kv_s = sbase + C::KV_OFF;
+    float* merge = reinterpret_cast<float*>(sp8 + C::MERGE_OFF);
+    const uint32_t bar0 = sbase + C::BAR_OFF;
+    int* stage_col = reinterpret_cast<int*>(sp8 + C::META_OFF);
+    int4* winfo = reinterpret_cast<int4*>(sp8 + C::WINFO_OFF);
+    auto full = [&](uint32_t s) { return bar0 + 8u * s; };
+    auto empty = [&](uint32_t s) { return bar0 + 8u * (S + s); };
+    auto qfull = [&](uint32_t q) { return bar0 + 8u * (2 * S + q); };
+    auto qempty = [&](uint32_t q) { return bar0 + 8u * (2 * S + 2 + q); };
+    const uint32_t mfull = bar0 + 8u * (2 * S + 4);
+    const uint32_t mempty = bar0 + 8u * (2 * S + 5);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const ErrorSink err{&p.hdr->abort, &p.hdr->status};
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), HG);
+        }
+        for (int q = 0; q < 2; ++q) {
+            mbar_init(qfull(q), 1);
+            mbar_init(qempty(q), kConsumerWarps);
+        }
+        mbar_init(mfull, C::SPLITS > 1 ? (C::SPLITS - 1) * HG : 1);
+        mbar_init(mempty, HG);
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ------------------------------------------------------ producer --
+        if (lane == 0) {
+            tma_prefetch_desc(&tmQ);
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+        }
+        const int total = p.num_items * p.groups;
+        uint32_t it = 0;  // K/V stages issued
+        int k = 0;        // windows published
+        bool aborted = false;
+        int item = 0;
+        if (lane == 0) item = atomicAdd(&p.hdr->counter, 1);
+        item = __shfl_sync(0xffffffffu, item, 0);
+        for (;;) {
+            const bool end = item >= total;
+            int w = -1, g = 0, b0 = 0, b1 = 0, nxt = total;
+            if (!end) {
+                if (lane == 0) nxt = atomicAdd(&p.hdr->counter, 1);
+                const int slot = item / p.groups;
+                g = item - slot * p.groups;
+                w = __ldg(p.order + slot);
+                if (w < p.q_window_base || w >= p.q_window_base + p.q_windows) {
+                    if (lane == 0) raise_error(err, F3S_ERR_BAD_FORMAT);
+                    aborted = true;
+                    break;
+                }
+                b0 = __ldg(p.offsets + w);
+                b1 = __ldg(p.offsets + w + 1);
+            }
+            const int q = k & 1;
+            if (!wait_warp(qempty(q), ((k >> 1) & 1) ^ 1, err, p.timeout_ns)) {
+                aborted = true;
+                break;
+            }
+            const int z0 = g * C::HC;
+            if (lane == 0) {
+                if (end) {
+                    winfo[q] = make_int4(-1, 0, 0, 0);
+                    mbar_arrive(qfull(q));
+                } else {
+                    winfo[q] = make_int4(w, g, b0, b1);
+                    if (b1 > b0) {
+                        mbar_arrive_expect_tx(qfull(q), C::TILE);
+                        load_tile<C::HC>(&tmQ, q_s + q * C::TILE, qfull(q), 16 * (w - p.q_window_base), z0,
+                                         p.tma3d);
+                    } else {
+                        mbar_arrive(qfull(q));
+                    }
+                }
+            }
+            if (end) break;
+            ++k;
+            for (int base = b0; base < b1 && !aborted; base += 32) {
+                const int n = min(32, b1 - base);
+                const int myc = lane < n ? __ldg(p.cols + base + lane) : 0;
+                if (__any_sync(0xffffffffu, myc < 0 || myc >= p.nrw_total)) {
+                    if (lane == 0) raise_error(err, F3S_ERR_BAD_FORMAT);
+                    aborted = true;
+                    break;
+                }
+                for (int i = 0; i < n; ++i) {
+                    const int c = __shfl_sync(0xffffffffu, myc, i);
+                    const uint32_t s = it % S;
+                    if (!wait_warp(empty(s), ((it / S) & 1) ^ 1, err, p.timeout_ns)) {
+                        aborted = true;
+                        break;
+                    }
+                    if (lane == 0) {
+                        stage_col[s] = c;
+                        mbar_arrive_expect_tx(full(s), 2 * C::TILE);
+                        const uint32_t dst = kv_s + s * 2 * C::TILE;
+                        load_tile<C::HC>(&tmK, dst, full(s), 16 * c, z0, p.tma3d);
+                        load_tile<C::HC>(&tmV, dst + C::TILE, full(s), 16 * c, z0, p.tma3d);
+                    }
+                    ++it;
+                }
+            }
+            if (aborted) break;
+            item = __shfl_sync(0xffffffffu, nxt, 0);
+        }
+        if (aborted && lane == 0) {
+            // let this CTA's own bulk copies land before it exits
+            const uint32_t n = it < (uint32_t)S ? it : (uint32_t)S;
+            for (uint32_t j = it - n; j < it; ++j) mbar_drain(full(j % S), (j / S) & 1, 100000000ull);
+            for (int kk = k > 2 ? k - 2 : 0; kk < k; ++kk) mbar_drain(qfull(kk & 1), (kk >> 1) & 1, 100000000ull);
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------- consumers --
+    const int hh = warp % HG;
+    const int sp = warp / HG;
+    const int g4 = lane >> 2, t4 = lane & 3;
+    const int a_row = (lane & 7) + (((lane >> 3) & 1) << 3);  // ldmatrix rows for Q (A) and V (B, trans)
+    const int a_chk = lane >> 4;
+    const int b_row = (lane & 7) + ((lane >> 4) << 3);  // ldmatrix rows for K (B)
+    const int b_chk = (lane >> 3) & 1;
+    constexpr int KS = D / 16;  // k-steps of QK^T, and 16-column pairs of PV
+    constexpr int NT = D / 8;   // n-tiles of the O accumulator
+    uint32_t it = 0;
+    for (int k = 0;; ++k) {
+        const int q = k & 1;
+        if (!wait_warp(qfull(q), (k >> 1) & 1, err, p.timeout_ns)) return;
+        const int4 wi = winfo[q];
+        if (wi.x < 0) return;
+        const int w = wi.x, g = wi.y, nb = wi.w - wi.z;
+        uint32_t qa[KS][4];
+        if (nb > 0) {
+            const uint32_t qt = q_s + q * C::TILE;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                const uint32_t row = (hh * (D / 64) + ks / 4) * 16 + a_row;
+                ldsm_x4(qt + swz128(row, (ks & 3) * 2 + a_chk), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(qempty(q));
+
+        float o[NT][4];
+#pragma unroll
+        for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+        float m0 = -1e30f, m1 = -1e30f, l0 = 0.f, l1 = 0.f;  // m in log2 units
+        bool ok = true;
+        for (int j = sp; j < nb; j += C::SPLITS) {
+            const uint32_t idx = it + (uint32_t)j;
+            const uint32_t s = idx % S;
+            if (!wait_warp(full(s), (idx / S) & 1, err, p.timeout_ns)) {
+                ok = false;
+                break;
+            }
+            const uint32_t kt = kv_s + s * 2 * C::TILE;
+            const uint32_t vt = kt + C::TILE;
+            float sc[2][4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sc[0][i] = sc[1][i] = 0.f;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                const uint32_t row = (hh * (D / 64) + ks / 4) * 16 + b_row;
+                uint32_t k0, k1, k2, k3;
+                ldsm_x4(kt + swz128(row, (ks & 3) * 2 + b_chk), k0, k1, k2, k3);
+                mma_16816(sc[0], qa[ks], k0, k1);
+                mma_16816(sc[1], qa[ks], k2, k3);
+            }
+            if (p.tail != 0 && stage_col[s] == p.nrw_total - 1) {
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        if (nt * 8 + 2 * t4 + (i & 1) >= p.tail) sc[nt][i] = -INFINITY;
+            }
+            float mx0 = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+            float mx1 = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+            const float mn0 = fmaxf(m0, mx0 * kLog2e);
+            const float mn1 = fmaxf(m1, mx1 * kLog2e);
+            const float c0 = fast_exp2(m0 - mn0);
+            const float c1 = fast_exp2(m1 - mn1);
+            m0 = mn0;
+            m1 = mn1;
+            float pr[2][4];
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                pr[nt][0] = fast_exp2(fmaf(sc[nt][0], kLog2e, -mn0));
+                pr[nt][1] = fast_exp2(fmaf(sc[nt][1], kLog2e, -mn0));
+                pr[nt][2] = fast_exp2(fmaf(sc[nt][2], kLog2e, -mn1));
+                pr[nt][3] = fast_exp2(fmaf(sc[nt][3], kLog2e, -mn1));
+            }
+            l0 = fmaf(l0, c0, (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]));
+            l1 = fmaf(l1, c1, (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]));
+#pragma unroll
+            for (int jn = 0; jn < NT; ++jn) {
+                o[jn][0] *= c0;
+                o[jn][1] *= c0;
+                o[jn][2] *= c1;
+                o[jn][3] *= c1;
+            }
+            uint32_t pa[4];
+            pa[0] = pack_half2(pr[0][0], pr[0][1]);
+            pa[1] = pack_half2(pr[0][2], pr[0][3]);
+            pa[2] = pack_half2(pr[1][0], pr[1][1]);
+            pa[3] = pack_half2(pr[1][2], pr[1][3]);
+#pragma unroll
+            for (int jj = 0; jj < KS; ++jj) {
+                const uint32_t row = (hh * (D / 64) + jj / 4) * 16 + a_row;
+                uint32_t v0, v1, v2, v3;
+                ldsm_x4_t(vt + swz128(row, (jj & 3) * 2 + a_chk), v0, v1, v2, v3);
+                mma_16816(o[2 * jj], pa, v0, v1);
+                mma_16816(o[2 * jj + 1], pa, v2, v3);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty(s));
+        }
+        if (!ok) return;
+        it += (uint32_t)nb;
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+        if constexpr (C::SPLITS > 1) {
+            if (sp > 0) {
+                if (!wait_warp(mempty, (k & 1) ^ 1, err, p.timeout_ns)) return;
+                float* slot = merge + ((sp - 1) * HG + hh) * C::SLOT_F;
+#pragma unroll
+                for (int r = 0; r < NT * 4; ++r) slot[r * 32 + lane] = o[r >> 2][r & 3];
+                if (t4 == 0) {
+                    float4 ml = make_float4(m0, l0, m1, l1);
+                    *reinterpret_cast<float4*>(slot + 16 * D + g4 * 4) = ml;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(mfull);
+                continue;
+            }
+            if (!wait_warp(mfull, k & 1, err, p.timeout_ns)) return;
+#pragma unroll 1
+            for (int s2 = 1; s2 < C::SPLITS; ++s2) {
+                const float* slot = merge + ((s2 - 1) * HG + hh) * C::SLOT_F;
+                const float4 ml = *reinterpret_cast<const float4*>(slot + 16 * D + g4 * 4);
+                const float M0 = fmaxf(m0, ml.x), M1 = fmaxf(m1, ml.z);
+                const float a0 = fast_exp2(m0 - M0), b0s = fast_exp2(ml.x - M0);
+                const float a1 = fast_exp2(m1 - M1), b1s = fast_exp2(ml.z - M1);
+                l0 = l0 * a0 + ml.y * b0s;
+                l1 = l1 * a1 + ml.w * b1s;
+                m0 = M0;
+                m1 = M1;
+#pragma unroll
+                for (int r = 0; r < NT * 4; ++r) {
+                    const float other = slot[r * 32 + lane];
+                    const bool lo_row = (r & 3) < 2;
+                    o[r >> 2][r & 3] = o[r >> 2][r & 3] * (lo_row ? a0 : a1) + other * (lo_row ? b0s : b1s);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(mempty);
+        }
+
+        // ------------------------------------------------ normalise, store --
+        const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
+        const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+        const int h = g * HG + hh;
+        const int ra = 16 * w + g4, rb = ra + 8;
+        const int64_t sa = (int64_t)(ra - 16 * p.q_window_base), sb = sa + 8;
+        if (ra < p.num_nodes && sa < p.q_rows) {
+            float* dst = p.O + (sa * p.heads + h) * D + 2 * t4;
+#pragma unroll
+            for (int jn = 0; jn < NT; ++jn)
+                __stcs(reinterpret_cast<float2*>(dst + jn * 8), make_float2(o[jn][0] * inv0, o[jn][1] * inv0));
+        }
+        if (rb < p.num_nodes && sb < p.q_rows) {
+            float* dst = p.O + (sb * p.heads + h) * D + 2 * t4;
+#pragma unroll
+            for (int jn = 0; jn < NT; ++jn)
+                __stcs(reinterpret_cast<float2*>(dst + jn * 8), make_float2(o[jn][2] * inv1, o[jn][3] * inv1));
+        }
+    }
+}
+
+// ------------------------------------------------------------------ host --
+
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+// Tensor map over fp16 [rows, heads, head_dim] whose box is one node-tile of
+// `box_hc` 128-byte head-chunks: 3-D {64, rows, heads*head_dim/64} with the
+// head-chunk stride (128 B) below the node stride, or the 2-D fallback
+// {heads*head_dim, rows} with a {64, 16} box.
+static bool encode_map(CUtensorMap* m, const void* base, int rows, int heads, int head_dim, int box_hc,
+                       bool three_d) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint64_t row_bytes = (cuuint64_t)heads * head_dim * 2;
+    CUresult r;
+    if (three_d) {
+        cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)heads * head_dim / 64};
+        cuuint64_t strides[2] = {row_bytes, 128};
+        cuuint32_t box[3] = {64, 16, (cuuint32_t)box_hc};
+        cuuint32_t es[3] = {1, 1, 1};
+        r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+        cuuint64_t dims[2] = {(cuuint64_t)heads * head_dim, (cuuint64_t)rows};
+        cuuint64_t strides[1] = {row_bytes};
+        cuuint32_t box[2] = {64, 16};
+        cuuint32_t es[2] = {1, 1};
+        r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    return r == CUDA_SUCCESS;
+}
+
+// Per-device, per-variant "max dynamic shared memory" attribute.
+template <int D, int HG>
+static int ensure_smem_attr() {
+    static int done[64] = {};
+    int dev = 0;
+    F3S_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 64 && done[dev]) return F3S_SUCCESS;
+    F3S_CUDA_TRY(cudaFuncSetAttribute(k_fused3s<D, HG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      FwdCfg<D, HG>::SMEM));
+    if (dev < 64) done[dev] = 1;
+    return F3S_SUCCESS;
+}
+
+static int g_tma_mode = -1;  // -1 unknown, 1 three-d maps accepted, 0 two-d fallback
+
+template <int D, int HG>
+static int launch_variant(const void* Q, const void* K, const void* V, FwdParams prm, int q_rows,
+                          cudaStream_t stream) {
+    using C = FwdCfg<D, HG>;
+    int rc = ensure_smem_attr<D, HG>();
+    if (rc != F3S_SUCCESS) return rc;
+    CUtensorMap mq, mk, mv;
+    bool three = g_tma_mode != 0;
+    bool okq = encode_map(&mq, Q, q_rows, prm.heads, D, C::HC, three);
+    if (!okq && three) {  // driver refused the 3-D form: fall back for good
+        three = false;
+        g_tma_mode = 0;
+        okq = encode_map(&mq, Q, q_rows, prm.heads, D, C::HC, false);
+    }
+    if (!okq || !encode_map(&mk, K, prm.num_nodes, prm.heads, D, C::HC, three) ||
+        !encode_map(&mv, V, prm.num_nodes, prm.heads, D, C::HC, three))
+        return F3S_ERR_INVALID_VALUE;
+    if (three) g_tma_mode = 1;
+    prm.tma3d = three ? 1 : 0;
+    const int items = prm.num_items * prm.groups;
+    const int grid = std::max(1, std::min(items, num_sms_of_current_device()));
+    k_fused3s<D, HG><<<grid, kFwdThreads, C::SMEM, stream>>>(mq, mk, mv, prm);
+    F3S_LAUNCH_CHECK();
+    return F3S_SUCCESS;
+}
+
+// Heads per CTA: the largest power of two <= min(8, 512 / head_dim) that
+// divides `heads` (so one tile is at most 16 KB and STAGES >= 4).
+static int pick_head_group(int heads, int head_dim) {
+    int cap = std::min(8, 512 / head_dim);
+    int hg = 1;
+    while (hg * 2 <= cap && heads % (hg * 2) == 0) hg *= 2;
+    return hg;
+}
+
+int forward_impl(const void* Q, const void* K, const void* V, float* O, const int* offsets, const int* cols,
+                 const int* order, int num_items, int num_nodes, int heads, int head_dim, int q_window_base,
+                 int q_rows, void* ws, size_t ws_bytes, cudaStream_t stream, uint64_t timeout_ns) {
+    if (num_items < 0 || num_nodes < 0 || heads <= 0 || q_window_base < 0 || q_rows < 0)
+        return F3S_ERR_INVALID_VALUE;
+    if (head_dim != 64 && head_dim != 128) return F3S_ERR_UNSUPPORTED;
+    if (!ws) return F3S_ERR_INVALID_VALUE;
+    if (ws_bytes < kWsHeaderBytes) return F3S_ERR_WORKSPACE;
+    if ((int64_t)heads * head_dim * 2 * 16 > (int64_t)1 << 40) return F3S_ERR_TOO_LARGE;
+    if (num_items == 0 || num_nodes == 0 || q_rows == 0) return F3S_SUCCESS;
+    if (!Q || !K || !V || !O || !offsets || !cols || !order) return F3S_ERR_INVALID_VALUE;
+    auto misaligned = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) != 0; };
+    if (misaligned(Q) || misaligned(K) || misaligned(V) || misaligned(O)) return F3S_ERR_INVALID_VALUE;
+    const int hg = pick_head_group(heads, head_dim);
+    FwdParams prm{};
+    prm.O = O;
+    prm.offsets = offsets;
+    prm.cols = cols;
+    prm.order = order;
+    prm.hdr = static_cast<WsHeader*>(ws);
+    prm.timeout_ns = timeout_ns;
+    prm.num_items = num_items;
+    prm.groups = heads / hg;
+    prm.num_nodes = num_nodes;
+    prm.nrw_total = (int)(((int64_t)num_nodes + 15) / 16);
+    prm.heads = heads;
+    prm.q_window_base = q_window_base;
+    prm.q_windows = (int)(((int64_t)q_rows + 15) / 16);
+    prm.q_rows = q_rows;
+    prm.tail = num_nodes & 15;
+    if ((int64_t)num_items * prm.groups > INT32_MAX) return F3S_ERR_TOO_LARGE;
+    // zero the abort flag and the ticket counter (adjacent words); the
+    // status word stays sticky
+    F3S_CUDA_TRY(cudaMemsetAsync(ws, 0, 2 * sizeof(int), stream));
+    if (head_dim == 64) {
+        switch (hg) {
+            case 1: return launch_variant<64, 1>(Q, K, V, prm, q_rows, stream);
+            case 2: return launch_variant<64, 2>(Q, K, V, prm, q_rows, stream);
+            case 4: return launch_variant<64, 4>(Q, K, V, prm, q_rows, stream);
+            default: return launch_variant<64, 8>(Q, K, V, prm, q_rows, stream);
+        }
+    }
+    switch (hg) {
+        case 1: return launch_variant<128, 1>(Q, K, V, prm, q_rows, stream);
+        case 2: return launch_variant<128, 2>(Q, K, V, prm, q_rows, stream);
+        default: return launch_variant<128, 4>(Q, K, V, prm, q_rows, stream);
+    }
+}
+
+// -------------------------------------------------- failure-path self-test --
+__global__ void k_wait_selftest(WsHeader* hdr, uint64_t timeout_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    const uint32_t b = smem_addr(&bar);
+    if (threadIdx.x == 0) {
+        mbar_init(b, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const ErrorSink err{&hdr->abort, &hdr->status};
+        // nobody arrives: the bounded wait gives up and records the timeout
+        mbar_wait_bounded(b, 0, err, timeout_ns);
+    }
+}
+
+int selftest_wait_timeout(uint64_t timeout_ns, void* ws, size_t ws_bytes, cudaStream_t stream) {
+    if (!ws) return F3S_ERR_INVALID_VALUE;
+    if (ws_bytes < kWsHeaderBytes) return F3S_ERR_WORKSPACE;
+    if (timeout_ns > 5ull * 1000 * 1000 * 1000) return F3S_ERR_INVALID_VALUE;
+    F3S_CUDA_TRY(cudaMemsetAsync(ws, 0, 2 * sizeof(int), stream));
+    k_wait_selftest<<<1, 32, 0, stream>>>(static_cast<WsHeader*>(ws), timeout_ns);
+    F3S_LAUNCH_CHECK();
+    return F3S_SUCCESS;
+}
+
+}  // namespace f3s
+
+extern "C" {
+
+size_t f3s_forward_workspace_size(void) { return f3s::kWsHeaderBytes; }
+
+int f3s_forward(const void* d_Q, const void* d_K, const void* d_V, float* d_O, const int32_t* d_window_offsets,
+                const int32_t* d_block_cols, const int32_t* d_order, int32_t num_items, int32_t num_nodes,
+                int32_t heads, int32_t head_dim, int32_t q_window_base, int32_t q_rows, void* d_workspace,
+                size_t workspace_bytes, f3s_stream_t stream) {
+    return f3s::forward_impl(d_Q, d_K, d_V, d_O, d_window_offsets, d_block_cols, d_order, num_items, num_nodes,
+                             heads, head_dim, q_window_base, q_rows, d_workspace, workspace_bytes,
+                             (cudaStream_t)stream, f3s::kWaitTimeoutNs);
+}
+
+int f3s_selftest_wait_timeout(uint64_t timeout_ns, void* d_workspace, size_t workspace_bytes, f3s_stream_t stream) {
+    return f3s::selftest_wait_timeout(timeout_ns, d_workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+}  // extern "C"

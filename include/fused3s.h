@@ -1,0 +1,167 @@
+/*
+ * fused3s.h -- C ABI of libfused3s.so, the B200 (sm_100a) fused 3S engine:
+ * CSR -> 16x16 block-sparse row windows -> descending-workload window order
+ * -> fused SDDMM + online softmax + SpMM -> fp32 O.
+ *
+ * Plain pointers and sizes only.  Every device pointer is caller-owned
+ * memory on the current device.  Every call is asynchronous on `stream`
+ * unless it says it synchronises.  Calls never exit the process: they return
+ * an f3s_status.  Errors found by a kernel (bad CSR, bad window id, an
+ * expired bounded wait) are recorded in the caller's workspace and read back
+ * with f3s_workspace_status().
+ *
+ * Reference interfaces replaced (paths relative to the fatalhawk/fused3S
+ * project root):
+ *   f3s_convert        <- blockSparseFormat convert_csr_to_block_sparse(
+ *                           int, const std::vector<int>&, const std::vector<int>&)
+ *                           src/converter.cu:13 (declared by callers at
+ *                           tests/test_fused_3s_v2.cu:10)
+ *   f3s_window_order   <- std::vector<int> generate_balanced_window_order(
+ *                           const blockSparseFormat&)   include/utils.cuh:48
+ *   f3s_forward        <- __global__ f3s_1tb1rw_kernel(...) src/fused3s_v2.cu:81-90,
+ *                           launched <<<nrw, dim3(32,4)>>> at
+ *                           tests/test_fused_3s_v2.cu:123-131
+ *   f3s_1tb1rw_launch  <- the same kernel with its exact argument list
+ *   f3s_half_from_float<- __global__ float2half_kernel tests/test_fused_3s_v2.cu:61-64
+ * The C++ header fused3s.hpp rebuilds the reference's own host API
+ * (GraphData, blockSparseFormat, load_csr_graph, ...) on top of these.
+ */
+#ifndef FUSED3S_H_
+#define FUSED3S_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without pulling in the CUDA headers. */
+typedef struct CUstream_st* f3s_stream_t;
+
+typedef enum f3s_status {
+    F3S_SUCCESS = 0,
+    F3S_ERR_INVALID_VALUE = 1, /* bad argument: null pointer, negative size ...   */
+    F3S_ERR_UNSUPPORTED = 2,   /* head_dim / heads combination not built          */
+    F3S_ERR_BAD_CSR = 3,       /* column outside [0, N) or row_ptr decreasing     */
+    F3S_ERR_WORKSPACE = 4,     /* workspace smaller than the *_workspace_size()   */
+    F3S_ERR_CUDA = 5,          /* a CUDA runtime call failed                      */
+    F3S_ERR_TIMEOUT = 6,       /* a bounded device-side wait expired              */
+    F3S_ERR_BAD_FORMAT = 7,    /* window id / block column outside its range      */
+    F3S_ERR_TOO_LARGE = 8      /* exceeds the int32 limits of the format          */
+} f3s_status;
+
+/* Human-readable name of a status code (static storage). */
+const char* f3s_status_string(int status);
+
+/* Library ABI version: major * 10000 + minor * 100 + patch. */
+int f3s_version(void);
+
+/* Last CUDA error seen by a call that returned F3S_ERR_CUDA (cudaError_t). */
+int f3s_last_cuda_error(void);
+
+/* ------------------------------------------------------------------------
+ * Workspace status.  Synchronises `stream`, returns the first error code a
+ * kernel recorded in `d_workspace` (any of the workspaces below) and clears
+ * it.  F3S_SUCCESS when none.
+ * ---------------------------------------------------------------------- */
+int f3s_workspace_status(void* d_workspace, f3s_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * CSR -> block-sparse row windows (src/converter.cu:13-44 semantics).
+ *
+ * Window w covers rows [16w, min(16w+16, N)); its active block columns are
+ * the sorted unique {v / 16} over the window's edges.  Output is bit-exact
+ * to the reference converter.
+ *
+ *   d_row_ptr        int32[num_nodes + 1]   CSR row pointers
+ *   d_col_ind        int32[nnz]             CSR column indices (any order)
+ *   d_window_offsets int32[nrw + 1] out     nrw = ceil(num_nodes / 16)
+ *   d_block_cols     int32[nnz]      out    capacity nnz (B <= nnz always);
+ *                                           first B entries are written
+ *   h_num_blocks     optional host int64 out: if non-NULL the call
+ *                    synchronises `stream`, checks the CSR status and stores
+ *                    B = window_offsets[nrw].
+ * The CSR is validated on the device (columns in [0, N), row_ptr
+ * non-decreasing and within [0, nnz]); a violation is reported as
+ * F3S_ERR_BAD_CSR (immediately when h_num_blocks != NULL, else through
+ * f3s_workspace_status).
+ * ---------------------------------------------------------------------- */
+size_t f3s_convert_workspace_size(int32_t num_nodes, int64_t nnz);
+int f3s_convert(const int32_t* d_row_ptr, const int32_t* d_col_ind, int32_t num_nodes, int64_t nnz,
+                int32_t* d_window_offsets, int32_t* d_block_cols, void* d_workspace,
+                size_t workspace_bytes, int64_t* h_num_blocks, f3s_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Balanced window order (include/utils.cuh:48-59 semantics).
+ *
+ * d_order[i] = window ids sorted by block count, descending; ties by
+ * ascending window id (a stable sort).  The block-count sequence along the
+ * order equals the reference's for every input.
+ * ---------------------------------------------------------------------- */
+size_t f3s_window_order_workspace_size(int32_t num_row_windows);
+int f3s_window_order(const int32_t* d_window_offsets, int32_t num_row_windows, int32_t* d_order,
+                     void* d_workspace, size_t workspace_bytes, f3s_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Fused SDDMM + online softmax + SpMM (src/fused3s_v2.cu:81-246 semantics,
+ * with columns >= num_nodes masked like the reference's CPU ground truth,
+ * tests/test_fused_3s_v2.cu:32-37).
+ *
+ * For every window w listed in d_order[0 .. num_items) and every head h:
+ *   O[r, h, :] = sum_c softmax_c(Q[r, h, :] . K[c, h, :]) V[c, h, :]
+ * over the 16 columns of every active block of w, rows r of w with r < N.
+ *
+ *   d_Q     fp16 [q_rows, heads, head_dim]  rows 16*q_window_base ... of Q
+ *   d_K,d_V fp16 [num_nodes, heads, head_dim]
+ *   d_O     fp32 [q_rows, heads, head_dim]  same rows as d_Q; rows of listed
+ *           windows are fully written (zeros for a window with no block)
+ *   d_window_offsets / d_block_cols: the converter's output for all windows
+ *   d_order  int32[num_items] window ids to compute (any subset, any order;
+ *            each must lie in [q_window_base, q_window_base + ceil(q_rows/16)))
+ *   q_window_base / q_rows: 0 / num_nodes on one GPU; a rank's slab when the
+ *            windows are sharded across GPUs.
+ * head_dim in {64, 128}; heads >= 1.  No padding of any tensor is needed:
+ * rows >= num_nodes are never read or written.  All base pointers must be
+ * 16-byte aligned.
+ * ---------------------------------------------------------------------- */
+size_t f3s_forward_workspace_size(void);
+int f3s_forward(const void* d_Q, const void* d_K, const void* d_V, float* d_O,
+                const int32_t* d_window_offsets, const int32_t* d_block_cols, const int32_t* d_order,
+                int32_t num_items, int32_t num_nodes, int32_t heads, int32_t head_dim,
+                int32_t q_window_base, int32_t q_rows, void* d_workspace, size_t workspace_bytes,
+                f3s_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Drop-in launch with the reference kernel's exact argument list
+ * (src/fused3s_v2.cu:81-90): Q/K/V/O have num_row_windows*16 rows of
+ * feat_dim columns, one head, and every one of those rows is treated as a
+ * real node (the reference v2 kernel cannot know N, so padded columns are
+ * not masked -- call f3s_forward with the true num_nodes for masking).
+ * Uses a library-owned per-device workspace (allocated on first use).
+ * ---------------------------------------------------------------------- */
+int f3s_1tb1rw_launch(const void* Q, const void* K, const void* V, float* O_out,
+                      const int32_t* window_offsets, const int32_t* block_col_indices,
+                      const int32_t* window_order, int32_t num_row_windows, int32_t feat_dim,
+                      f3s_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * fp32 -> fp16 (round to nearest even), n elements
+ * (tests/test_fused_3s_v2.cu:61-64).
+ * ---------------------------------------------------------------------- */
+int f3s_half_from_float(const float* d_in, void* d_out, int64_t n, f3s_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Self-test of the failure path: launches a kernel that waits on an
+ * mbarrier nobody arrives on, with the given bound.  The wait gives up,
+ * records F3S_ERR_TIMEOUT in the workspace and the kernel returns normally;
+ * read it with f3s_workspace_status().  No fault, trap or hang.
+ * ---------------------------------------------------------------------- */
+int f3s_selftest_wait_timeout(uint64_t timeout_ns, void* d_workspace, size_t workspace_bytes,
+                              f3s_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FUSED3S_H_ */

@@ -1,0 +1,63 @@
+"""The C-ABI library loads on a machine without a GPU and exports exactly
+what include/fused3s.h declares.  No compute call is made here."""
+import ctypes
+import re
+
+import pytest
+
+from conftest import ROOT
+from fused3s_b200 import _lib
+
+
+def declared_functions():
+    text = (ROOT / "include" / "fused3s.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(f3s_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_expected_surface():
+    names = declared_functions()
+    for must in ("f3s_convert", "f3s_window_order", "f3s_forward", "f3s_1tb1rw_launch",
+                 "f3s_workspace_status", "f3s_half_from_float"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+        assert isinstance(getattr(lib, name), ctypes._CFuncPtr)
+
+
+def test_python_binding_covers_the_header():
+    assert set(declared_functions()) == set(_lib.SIGNATURES)
+
+
+def test_host_only_queries(lib):
+    assert lib.f3s_version() >= 10000
+    assert lib.f3s_forward_workspace_size() == 256
+    assert lib.f3s_convert_workspace_size(2708, 13264) >= 256 + 4 * 13264
+    assert lib.f3s_convert_workspace_size(-1, 0) == 0
+    assert lib.f3s_window_order_workspace_size(1 << 20) > 4 * (1 << 20) * 4
+    for code in range(0, 9):
+        s = lib.f3s_status_string(code).decode()
+        assert s.startswith("F3S_")
+    assert "UNKNOWN" in lib.f3s_status_string(99).decode()
+
+
+def test_invalid_arguments_are_rejected_without_touching_the_gpu(lib):
+    # validated on the host before any CUDA call
+    assert lib.f3s_forward(None, None, None, None, None, None, None, 1, 10, 1, 96, 0, 10, None, 0,
+                           None) == _lib.F3S_ERR_UNSUPPORTED
+    assert lib.f3s_forward(None, None, None, None, None, None, None, 1, 10, 1, 64, 0, 10, None, 0,
+                           None) == _lib.F3S_ERR_INVALID_VALUE
+    assert lib.f3s_convert(None, None, -1, 0, None, None, None, 0, None, None) == _lib.F3S_ERR_INVALID_VALUE
+    assert lib.f3s_window_order(None, -3, None, None, 0, None) == _lib.F3S_ERR_INVALID_VALUE
+    assert lib.f3s_half_from_float(None, None, -1, None) == _lib.F3S_ERR_INVALID_VALUE
+
+
+def test_product_package_does_not_reference_the_oracle():
+    """The shipped package never imports or loads the oracle."""
+    pkg = ROOT / "fused3s_b200"
+    for path in list(pkg.glob("*.py")) + list((pkg / "csrc").glob("*")):
+        text = path.read_text()
+        assert "import oracle" not in text and "liboracle" not in text and "libf3s_ref" not in text, path

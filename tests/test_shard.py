@@ -1,0 +1,87 @@
+"""Multi-GPU host logic on CPU: the window partition, the per-rank order and
+the slab all-gather, the latter with two gloo ranks."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import oracle
+from fused3s_b200 import graphs as G
+from fused3s_b200 import shard
+
+
+def test_partition_covers_all_windows_contiguously():
+    rng = np.random.default_rng(0)
+    for world in (1, 2, 3, 4, 8):
+        cnt = rng.zipf(1.7, 5000).clip(max=20000)
+        off = np.concatenate([[0], np.cumsum(cnt)])
+        parts = shard.partition_windows(off, world)
+        assert len(parts) == world
+        assert parts[0][0] == 0 and parts[-1][1] == 5000
+        for (a, b), (c, d) in zip(parts[:-1], parts[1:]):
+            assert b == c and a <= b
+        cost = cnt + shard.WINDOW_COST
+        loads = [cost[a:b].sum() for a, b in parts]
+        # contiguous cuts are within one window's cost of the ideal share
+        assert max(loads) - cost.sum() / world <= cost.max() + 1e-9
+
+
+def test_partition_more_ranks_than_windows():
+    off = np.array([0, 3, 5])
+    parts = shard.partition_windows(off, 4)
+    assert parts[0][0] == 0 and parts[-1][1] == 2
+    assert sum(b - a for a, b in parts) == 2
+
+
+def test_rank_orders_partition_the_global_order():
+    g = G.make_graph("c2")
+    off, _ = oracle.convert(g.num_nodes, g.row_ptr, g.col_ind)
+    order = oracle.window_order(off)
+    parts = shard.partition_windows(off, 3)
+    got = [shard.rank_order(order, a, b) for a, b in parts]
+    assert sorted(np.concatenate(got).tolist()) == list(range(len(off) - 1))
+    cnt = np.diff(off)
+    for o in got:
+        assert np.all(np.diff(cnt[o]) <= 0)  # still descending
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _gather_worker(rank, world, port, result_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        n = 1003
+        full = torch.arange(n * 6, dtype=torch.float32).reshape(n, 2, 3)
+        off = np.concatenate([[0], np.cumsum(np.random.default_rng(1).integers(0, 9, (n + 15) // 16))])
+        parts = shard.partition_windows(off, world)
+        slabs = [shard.slab_rows(a, b, n) for a, b in parts]
+        r0, r1 = slabs[rank]
+        got = shard.gather_rows(full[r0:r1].clone(), slabs)
+        result_q.put((rank, bool(torch.equal(got, full))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_rows_two_gloo_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert sorted(results) == [(0, True), (1, True)]
