@@ -129,7 +129,7 @@ def build_workload(config: str, device):
     from fused3s_b200 import graphs as G
     cfg = G.CONFIGS[config]
     t0 = time.time()
-    g = G.make_graph(config, device=str(device) if config in ("c4", "c5") else "cpu")
+    g = G.make_graph(config, device=str(device) if config in ("c4", "c5", "c4s") else "cpu")
     log(f"[bench] graph {config}: N={g.num_nodes} E={g.num_edges} ({time.time() - t0:.1f}s)")
     return g, cfg
 
@@ -218,7 +218,7 @@ def run_reference(args):
     import oracle
     config = args.config
     cfg = G.CONFIGS[config]
-    g = G.make_graph(config, device="cuda" if (config in ("c4", "c5") and torch.cuda.is_available()) else "cpu")
+    g = G.make_graph(config, device="cuda" if (config in ("c4", "c5", "c4s") and torch.cuda.is_available()) else "cpu")
     conv = oracle.ref_convert if oracle.ref_available() else oracle.convert
     off, cols = conv(g.num_nodes, g.row_ptr, g.col_ind)
     B, nrw = int(cols.shape[0]), len(off) - 1
@@ -451,7 +451,7 @@ def main(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c4", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--config", default="c4", choices=["c1", "c2", "c3", "c4", "c5", "c4s"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gather", action="store_true", help="also time the NCCL all-gather of O (N > 1)")
     ap.add_argument("--no-e2e", action="store_true")

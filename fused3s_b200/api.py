@@ -54,6 +54,16 @@ class BlockSparseFormat:
     window_offsets: torch.Tensor     # int32 [nrw + 1] on the GPU
     block_col_indices: torch.Tensor  # int32 [B] on the GPU
     num_nodes: int
+    # buffer behind block_col_indices (never empty, so its pointer is valid
+    # even for a graph without edges)
+    storage: Optional[torch.Tensor] = None
+
+    @property
+    def cols_ptr(self) -> int:
+        buf = self.storage if self.storage is not None else self.block_col_indices
+        if buf.numel() == 0:
+            buf = self.storage = torch.zeros(1, dtype=torch.int32, device=buf.device)
+        return buf.data_ptr()
 
     @property
     def num_blocks(self) -> int:
@@ -151,7 +161,7 @@ def convert_csr_to_block_sparse(num_nodes: int, row_ptr, col_ind, device=None) -
         st = lib.f3s_convert(_ptr(rp), _ptr(ci) if nnz else None, num_nodes, nnz, _ptr(offsets),
                              _ptr(cols), _ptr(ws), ws.numel(), nb, _stream_ptr(device))
     check(st, "f3s_convert")
-    return BlockSparseFormat(nrw, offsets, cols[: nb.value], num_nodes)
+    return BlockSparseFormat(nrw, offsets, cols[: nb.value], num_nodes, storage=cols)
 
 
 def generate_balanced_window_order(fmt: BlockSparseFormat) -> torch.Tensor:
@@ -222,7 +232,7 @@ def fused3s_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: Bloc
     ws = _WS.get(device, "forward", lib.f3s_forward_workspace_size())
     with torch.cuda.device(device):
         st = lib.f3s_forward(_ptr(Q), _ptr(K), _ptr(V), _ptr(out), _ptr(fmt.window_offsets),
-                             _ptr(fmt.block_col_indices), _ptr(order), int(order.numel()), num_nodes, heads,
+                             fmt.cols_ptr, _ptr(order), int(order.numel()), num_nodes, heads,
                              head_dim, q_window_base, q_rows, _ptr(ws), ws.numel(), _stream_ptr(device))
         check(st, "f3s_forward")
         if check_status:

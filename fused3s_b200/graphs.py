@@ -59,6 +59,9 @@ CONFIGS = {
     "c3": Config("c3", 8, 64, "normal", "4096 ER graphs (20-500 nodes, deg 8)+self-loops, H=8 d=64"),
     "c4": Config("c4", 8, 64, "normal", "R-MAT N=2^20 avg deg 16 symmetrised permuted, H=8 d=64"),
     "c5": Config("c5", 4, 128, "normal", "R-MAT N=2^24 avg deg 32 symmetrised permuted, H=4 d=128"),
+    # C4's family at 2^18 nodes: K+V still exceed L2 (512 MB) while the whole
+    # case holds ~2 GB on the device -- the size used for ncu captures
+    "c4s": Config("c4s", 8, 64, "normal", "R-MAT N=2^18 avg deg 16 symmetrised permuted, H=8 d=64"),
 }
 
 
@@ -237,6 +240,8 @@ def make_graph(config: str, device: str = "cpu", seed: Optional[int] = None) -> 
         return rmat_graph(20, 16, device=device, name="c4", **kw)
     if config == "c5":
         return rmat_graph(24, 32, device=device, name="c5", **kw)
+    if config == "c4s":
+        return rmat_graph(18, 16, device=device, name="c4s", **kw)
     raise ValueError(f"unknown config {config!r}")
 
 
