@@ -36,6 +36,7 @@ SIGNATURES = {
     "f3s_workspace_status": (ctypes.c_int, [_P, _P]),
     "f3s_convert_workspace_size": (_SZ, [_I32, _I64]),
     "f3s_convert": (ctypes.c_int, [_P, _P, _I32, _I64, _P, _P, _P, _SZ, ctypes.POINTER(_I64), _P]),
+    "f3s_convert_noalloc": (ctypes.c_int, [_P, _P, _I32, _I64, _P, _P, ctypes.POINTER(_I64), _P]),
     "f3s_window_order_workspace_size": (_SZ, [_I32]),
     "f3s_window_order": (ctypes.c_int, [_P, _I32, _P, _P, _SZ, _P]),
     "f3s_forward_workspace_size": (_SZ, []),

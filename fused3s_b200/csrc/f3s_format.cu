@@ -10,6 +10,7 @@
 // per-window work of the converter stays in shared memory.
 #include <algorithm>
 #include <climits>
+#include <mutex>
 #include "f3s_internal.cuh"
 
 namespace f3s {
@@ -514,9 +515,73 @@ static int window_order_impl(const int32_t* d_offsets, int32_t nrw, int32_t* d_o
     return F3S_SUCCESS;
 }
 
+// =========================================================================
+// Converter for callers that cannot allocate device memory.
+//
+// Its scratch lives in the library itself: a fixed 32 MiB array in device
+// global memory that every GPU loading this library holds until the process
+// exits.  Host code only ever sees a host-side stand-in for the array's name,
+// so the real device address is looked up once per device, with that device
+// current, through cudaGetSymbolAddress.  Every call shares the array;
+// calls whose work overlaps on the GPU (other streams, other host threads)
+// race on it.
+// =========================================================================
+
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static int noalloc_scratch_address(void** out) {
+    static void* addr[64] = {};
+    static std::mutex mu;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        note_cuda_error(e);
+        return F3S_ERR_CUDA;
+    }
+    if (dev < 0 || dev >= 64) return F3S_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            note_cuda_error(e);
+            return F3S_ERR_CUDA;
+        }
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return F3S_SUCCESS;
+}
+
+static int convert_noalloc_impl(const int32_t* d_row_ptr, const int32_t* d_col_ind, int32_t num_nodes,
+                                int64_t nnz, int32_t* d_window_offsets, int32_t* d_block_cols,
+                                int64_t* h_num_blocks, cudaStream_t stream) {
+    if (num_nodes < 0 || nnz < 0 || h_num_blocks == nullptr) return F3S_ERR_INVALID_VALUE;
+    if (nnz > INT_MAX) return F3S_ERR_TOO_LARGE;
+    if (convert_layout(num_nodes, nnz).total > kNoAllocScratchBytes) return F3S_ERR_WORKSPACE;
+    void* ws = nullptr;
+    int rc = noalloc_scratch_address(&ws);
+    if (rc != F3S_SUCCESS) return rc;
+    // the array keeps the previous call's contents: the header (abort flag,
+    // heavy-window counter, status word) must start at zero; everything
+    // after it is written before it is read within one call
+    F3S_CUDA_TRY(cudaMemsetAsync(ws, 0, kWsHeaderBytes, stream));
+    return convert_impl(d_row_ptr, d_col_ind, num_nodes, nnz, d_window_offsets, d_block_cols, ws,
+                        kNoAllocScratchBytes, h_num_blocks, stream);
+}
+
 }  // namespace f3s
 
 extern "C" {
+
+int f3s_convert_noalloc(const int32_t* d_row_ptr, const int32_t* d_col_ind, int32_t num_nodes, int64_t nnz,
+                        int32_t* d_window_offsets, int32_t* d_block_cols, int64_t* h_num_blocks,
+                        f3s_stream_t stream) {
+    return f3s::convert_noalloc_impl(d_row_ptr, d_col_ind, num_nodes, nnz, d_window_offsets, d_block_cols,
+                                     h_num_blocks, (cudaStream_t)stream);
+}
 
 size_t f3s_convert_workspace_size(int32_t num_nodes, int64_t nnz) {
     if (num_nodes < 0 || nnz < 0) return 0;

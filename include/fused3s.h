@@ -93,6 +93,38 @@ int f3s_convert(const int32_t* d_row_ptr, const int32_t* d_col_ind, int32_t num_
                 size_t workspace_bytes, int64_t* h_num_blocks, f3s_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * CSR -> block-sparse row windows without any device allocation.
+ * No counterpart in the reference (its converter runs on the host).
+ *
+ * Same output and CSR checks as f3s_convert, for callers that cannot
+ * allocate device memory for the converter's scratch: a plugin inside a
+ * framework whose caching allocator has already reserved the GPU's memory
+ * (a cudaMalloc of its own may fail there, or take memory the framework
+ * thinks it owns), or a latency-critical service that allocates everything
+ * at start-up and never calls cudaMalloc / cudaFree afterwards (both can
+ * stall or synchronise the device).  The caller still passes the inputs and
+ * the outputs (d_window_offsets: nrw + 1 entries, d_block_cols: nnz).
+ *
+ * The scratch is a fixed 32 MiB array inside the library, in device memory,
+ * held by every GPU that loads the library until the process exits.  A
+ * graph whose f3s_convert_workspace_size(num_nodes, nnz) exceeds 32 MiB
+ * (about nnz + 2 * num_nodes / 16 > 8.3 million) is rejected with
+ * F3S_ERR_WORKSPACE before anything runs.  This call itself allocates
+ * nothing (no cudaMalloc, cudaFree or allocating library routine).
+ *
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current); make that first call
+ * before any stream capture.  h_num_blocks is required: the call
+ * synchronises `stream`, reads the kernels' status from the shared array and
+ * returns it (F3S_ERR_BAD_CSR etc.), and stores B.  All calls share the one
+ * array, so calls whose work overlaps on the GPU (from several streams or
+ * host threads) race; serialise them.
+ * ---------------------------------------------------------------------- */
+int f3s_convert_noalloc(const int32_t* d_row_ptr, const int32_t* d_col_ind, int32_t num_nodes, int64_t nnz,
+                        int32_t* d_window_offsets, int32_t* d_block_cols, int64_t* h_num_blocks,
+                        f3s_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Balanced window order (include/utils.cuh:48-59 semantics).
  *
  * d_order[i] = window ids sorted by block count, descending; ties by
