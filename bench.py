@@ -295,11 +295,21 @@ def run_ours(args):
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
     n_items = int(my_order.numel())
+    # L2 eviction hints per block column: computed once per graph and rank
+    hints = None
+    hints_ms = None
+    if args.l2_hints == "on":
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        hints = F.column_hints(fmt, H, d, order=my_order)
+        torch.cuda.synchronize()
+        hints_ms = (time.perf_counter() - t0) * 1e3
+    hints_ptr = hints.data_ptr() if hints is not None else None
 
     def step():
         st = lib.f3s_forward(Q.data_ptr(), Kf.data_ptr(), Vf.data_ptr(), O.data_ptr(),
-                             fmt.window_offsets.data_ptr(), fmt.block_col_indices.data_ptr(),
-                             my_order.data_ptr(), n_items, N, H, d, lo, r1 - r0, ws.data_ptr(), ws.numel(), sptr)
+                             fmt.window_offsets.data_ptr(), fmt.cols_ptr, my_order.data_ptr(), hints_ptr,
+                             n_items, N, H, d, lo, r1 - r0, ws.data_ptr(), ws.numel(), sptr)
         if st != 0:
             raise _lib.Fused3SError(st, "f3s_forward")
 
@@ -354,7 +364,7 @@ def run_ours(args):
             dQ.copy_(hQ, non_blocking=True)
             dK.copy_(hK, non_blocking=True)
             dV.copy_(hV, non_blocking=True)
-            F.fused3s_forward(dQ, dK, dV, fmt, order=my_order, out=O, q_window_base=lo)
+            F.fused3s_forward(dQ, dK, dV, fmt, order=my_order, out=O, q_window_base=lo, col_hints=hints)
             hO.copy_(O, non_blocking=True)
 
         for _ in range(max(1, args.warmup // 2)):
@@ -426,7 +436,8 @@ def run_ours(args):
                        "parallelism": f"row-window shards x{world}, K/V replicated",
                        "l2": "inputs larger than L2" if (Kf.numel() + Vf.numel()) * 2 > 126e6 else
                              "inputs fit in L2 (no flush)",
-                       "convert_ms": convert_ms, "order_ms": order_ms},
+                       "convert_ms": convert_ms, "order_ms": order_ms, "l2_hints": args.l2_hints,
+                       "hints_ms": hints_ms},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "traffic": traffic, "peak_kind": peak_kind,
                          "alg_bytes_per_launch": bytes_launch, "kernel_ms": kern_ms,
@@ -454,6 +465,8 @@ def main(argv=None):
     ap.add_argument("--config", default="c4", choices=["c1", "c2", "c3", "c4", "c5", "c4s"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gather", action="store_true", help="also time the NCCL all-gather of O (N > 1)")
+    ap.add_argument("--l2-hints", default="on", choices=["on", "off"],
+                    help="per block column L2 eviction hints (computed once per graph)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU work for cpu_baseline")

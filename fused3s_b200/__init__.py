@@ -9,6 +9,7 @@ from .api import (
     BlockSparseFormat,
     GraphData,
     Fused3SError,
+    column_hints,
     convert_csr_to_block_sparse,
     f3s_1tb1rw_kernel,
     float2half,
@@ -23,6 +24,7 @@ __all__ = [
     "BlockSparseFormat",
     "GraphData",
     "Fused3SError",
+    "column_hints",
     "convert_csr_to_block_sparse",
     "f3s_1tb1rw_kernel",
     "float2half",

@@ -197,9 +197,33 @@ def _as_nhd(t: torch.Tensor) -> torch.Tensor:
     return t.unsqueeze(1) if t.dim() == 2 else t
 
 
+def column_hints(fmt: BlockSparseFormat, heads: int, head_dim: int, order: Optional[torch.Tensor] = None,
+                 l2_fraction: float = 0.5) -> torch.Tensor:
+    """Per block column L2 eviction hints (uint8[nrw]) for the windows in
+    `order` (default: all): the most popular columns that fit in
+    `l2_fraction` of the device's L2 are kept, single-use columns streamed.
+    Computed once per graph; pass to fused3s_forward(col_hints=...)."""
+    lib = _lib.load()
+    device = fmt.window_offsets.device
+    nrw = fmt.num_row_windows
+    if order is None:
+        order = torch.arange(nrw, dtype=torch.int32, device=device)
+    order = order.to(device=device, dtype=torch.int32).contiguous()
+    hints = torch.zeros(max(nrw, 1), dtype=torch.uint8, device=device)
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    ws = _WS.get(device, "hints", lib.f3s_column_hints_workspace_size(nrw))
+    with torch.cuda.device(device):
+        st = lib.f3s_column_hints(_ptr(fmt.window_offsets), fmt.cols_ptr, _ptr(order), int(order.numel()), nrw,
+                                  16 * heads * head_dim * 2 * 2, int(l2 * l2_fraction), _ptr(hints), _ptr(ws),
+                                  ws.numel(), _stream_ptr(device))
+    check(st, "f3s_column_hints")
+    return hints[:nrw]
+
+
 def fused3s_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: BlockSparseFormat,
                     order: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-                    q_window_base: int = 0, check_status: bool = False) -> torch.Tensor:
+                    q_window_base: int = 0, check_status: bool = False,
+                    col_hints: Optional[torch.Tensor] = None) -> torch.Tensor:
     """O = block-sparse softmax(Q K^T) V, fused (the fused3s_v2 path).
 
     Q: fp16 [q_rows, H, d] (or [q_rows, d] for one head) holding rows
@@ -207,7 +231,10 @@ def fused3s_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: Bloc
     order: int32 window ids to compute (default: every window of the slab in
        the balanced order).  Returns fp32 O shaped like Q; rows of the listed
        windows are written in full (zeros for windows with no block).
-    check_status: synchronise and raise if a kernel recorded an error."""
+    check_status: synchronise and raise if a kernel recorded an error.
+    col_hints: optional uint8[nrw] from column_hints() (speed only)."""
+    if col_hints is not None and (col_hints.dtype != torch.uint8 or col_hints.numel() < fmt.num_row_windows):
+        raise ValueError("col_hints must be uint8 with one entry per row window")
     lib = _lib.load()
     _check_features(Q, K, V)
     q3, k3 = _as_nhd(Q), _as_nhd(K)
@@ -232,7 +259,7 @@ def fused3s_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: Bloc
     ws = _WS.get(device, "forward", lib.f3s_forward_workspace_size())
     with torch.cuda.device(device):
         st = lib.f3s_forward(_ptr(Q), _ptr(K), _ptr(V), _ptr(out), _ptr(fmt.window_offsets),
-                             fmt.cols_ptr, _ptr(order), int(order.numel()), num_nodes, heads,
+                             fmt.cols_ptr, _ptr(order), _ptr(col_hints), int(order.numel()), num_nodes, heads,
                              head_dim, q_window_base, q_rows, _ptr(ws), ws.numel(), _stream_ptr(device))
         check(st, "f3s_forward")
         if check_status:

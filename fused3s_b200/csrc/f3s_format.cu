@@ -516,6 +516,112 @@ static int window_order_impl(const int32_t* d_offsets, int32_t nrw, int32_t* d_o
 }
 
 // =========================================================================
+// L2 eviction hints per block column.
+//
+// A block column's K/V tile is read once per window that lists it.  Columns
+// listed by many windows are worth keeping in L2; columns listed by a single
+// window are never reused.  popularity[c] = number of listed windows that
+// reference c; the most popular columns, up to an L2 byte budget, get hint 1
+// (evict-last), single-use columns hint 2 (evict-first), the rest hint 0.
+//   k_hint_popularity  one warp per listed window, atomics per block
+//   k_hint_histogram   histogram of min(popularity, 4095)
+//   k_hint_threshold   one thread: the smallest popularity whose columns
+//                      still fit the budget
+//   k_hint_mark        writes the hints
+// =========================================================================
+
+constexpr int kHintBins = 4096;
+
+__global__ void __launch_bounds__(256) k_hint_popularity(const int* __restrict__ offsets,
+                                                         const int* __restrict__ cols, const int* __restrict__ order,
+                                                         int num_items, int* __restrict__ pop) {
+    const int i = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (i >= num_items) return;
+    const int w = order[i];
+    const int b1 = offsets[w + 1];
+    for (int b = offsets[w] + lane; b < b1; b += 32) atomicAdd(&pop[cols[b]], 1);
+}
+
+__global__ void __launch_bounds__(256) k_hint_histogram(const int* __restrict__ pop, int nrw,
+                                                        int* __restrict__ hist) {
+    __shared__ int h[kHintBins];
+    for (int i = threadIdx.x; i < kHintBins; i += 256) h[i] = 0;
+    __syncthreads();
+    for (int c = blockIdx.x * 256 + threadIdx.x; c < nrw; c += gridDim.x * 256)
+        atomicAdd(&h[min(pop[c], kHintBins - 1)], 1);
+    __syncthreads();
+    for (int i = threadIdx.x; i < kHintBins; i += 256)
+        if (h[i]) atomicAdd(&hist[i], h[i]);
+}
+
+__global__ void k_hint_threshold(const int* __restrict__ hist, int64_t budget_cols, int* __restrict__ thr) {
+    if (threadIdx.x != 0) return;
+    int64_t cum = 0;
+    int t = kHintBins;  // nothing hot
+    for (int b = kHintBins - 1; b >= 2; --b) {
+        if (cum + hist[b] > budget_cols) break;
+        cum += hist[b];
+        t = b;
+    }
+    *thr = t;
+}
+
+__global__ void __launch_bounds__(256) k_hint_mark(const int* __restrict__ pop, int nrw,
+                                                   const int* __restrict__ thr, uint8_t* __restrict__ hints) {
+    const int t = *thr;
+    for (int c = blockIdx.x * 256 + threadIdx.x; c < nrw; c += gridDim.x * 256) {
+        const int p = pop[c];
+        hints[c] = (uint8_t)(p >= t ? 1 : (p == 1 ? 2 : 0));
+    }
+}
+
+struct HintLayout {
+    size_t pop, hist, thr, total;
+};
+
+static HintLayout hint_layout(int32_t nrw) {
+    HintLayout L;
+    size_t off = kWsHeaderBytes;
+    L.pop = off;
+    off = align_up(off + (size_t)std::max(nrw, 1) * 4, 256);
+    L.hist = off;
+    off = align_up(off + (size_t)kHintBins * 4, 256);
+    L.thr = off;
+    L.total = align_up(off + 4, 256);
+    return L;
+}
+
+static int column_hints_impl(const int32_t* d_offsets, const int32_t* d_cols, const int32_t* d_order,
+                             int32_t num_items, int32_t nrw, int64_t bytes_per_column, int64_t l2_budget_bytes,
+                             uint8_t* d_hints, void* d_workspace, size_t workspace_bytes, cudaStream_t stream) {
+    if (nrw < 0 || num_items < 0 || bytes_per_column <= 0 || l2_budget_bytes < 0) return F3S_ERR_INVALID_VALUE;
+    if (nrw == 0) return F3S_SUCCESS;
+    if (!d_offsets || !d_cols || !d_hints || !d_workspace || (num_items > 0 && !d_order))
+        return F3S_ERR_INVALID_VALUE;
+    const HintLayout L = hint_layout(nrw);
+    if (workspace_bytes < L.total) return F3S_ERR_WORKSPACE;
+    char* ws = static_cast<char*>(d_workspace);
+    int* pop = reinterpret_cast<int*>(ws + L.pop);
+    int* hist = reinterpret_cast<int*>(ws + L.hist);
+    int* thr = reinterpret_cast<int*>(ws + L.thr);
+    F3S_CUDA_TRY(cudaMemsetAsync(pop, 0, (size_t)nrw * 4, stream));
+    F3S_CUDA_TRY(cudaMemsetAsync(hist, 0, (size_t)kHintBins * 4, stream));
+    if (num_items > 0) {
+        k_hint_popularity<<<(num_items + 7) / 8, 256, 0, stream>>>(d_offsets, d_cols, d_order, num_items, pop);
+        F3S_LAUNCH_CHECK();
+    }
+    const int grid = std::max(1, std::min((nrw + 255) / 256, num_sms_of_current_device() * 4));
+    k_hint_histogram<<<grid, 256, 0, stream>>>(pop, nrw, hist);
+    F3S_LAUNCH_CHECK();
+    k_hint_threshold<<<1, 32, 0, stream>>>(hist, l2_budget_bytes / bytes_per_column, thr);
+    F3S_LAUNCH_CHECK();
+    k_hint_mark<<<grid, 256, 0, stream>>>(pop, nrw, thr, d_hints);
+    F3S_LAUNCH_CHECK();
+    return F3S_SUCCESS;
+}
+
+// =========================================================================
 // Converter for callers that cannot allocate device memory.
 //
 // Its scratch lives in the library itself: a fixed 32 MiB array in device
@@ -593,6 +699,19 @@ int f3s_convert(const int32_t* d_row_ptr, const int32_t* d_col_ind, int32_t num_
                 int64_t* h_num_blocks, f3s_stream_t stream) {
     return f3s::convert_impl(d_row_ptr, d_col_ind, num_nodes, nnz, d_window_offsets, d_block_cols,
                              d_workspace, workspace_bytes, h_num_blocks, (cudaStream_t)stream);
+}
+
+size_t f3s_column_hints_workspace_size(int32_t num_row_windows) {
+    if (num_row_windows < 0) return 0;
+    return f3s::hint_layout(num_row_windows).total;
+}
+
+int f3s_column_hints(const int32_t* d_window_offsets, const int32_t* d_block_cols, const int32_t* d_order,
+                     int32_t num_items, int32_t num_row_windows, int64_t bytes_per_column, int64_t l2_budget_bytes,
+                     uint8_t* d_col_hints, void* d_workspace, size_t workspace_bytes, f3s_stream_t stream) {
+    return f3s::column_hints_impl(d_window_offsets, d_block_cols, d_order, num_items, num_row_windows,
+                                  bytes_per_column, l2_budget_bytes, d_col_hints, d_workspace, workspace_bytes,
+                                  (cudaStream_t)stream);
 }
 
 size_t f3s_window_order_workspace_size(int32_t num_row_windows) {

@@ -14,16 +14,24 @@
 //     tail balances itself.
 //   * Memory layout is node-major [N, H, d] fp16.  A CTA takes HG heads of a
 //     window at once, so one active block's K (or V) tile is 16 * HG * d * 2
-//     contiguous bytes in HBM: a single TMA bulk-tensor load per tile
-//     (3-D tensor map {64 elems, node, head-chunk}, 128-byte swizzle) lands it
-//     in shared memory as [head-chunk][16 nodes][64 elems] rows of 128 B,
-//     ready for conflict-free ldmatrix.
+//     contiguous bytes in HBM.  It is fetched with at most two TMA boxes of
+//     a 3-D tensor map {64 elems, head-chunk, node} (strides grow with the
+//     dimension, as the driver documents; 128-byte swizzle): one of HA
+//     head-chunks, HA odd, and one of the remaining chunk.  In shared memory
+//     the tile is node-major with a node stride of HA * 128 B, an odd
+//     multiple of the swizzle row, so ldmatrix reads are conflict-free
+//     (chunk_row()).  The K and V boxes of a block are issued by separate
+//     lanes of the producer warp in one instruction.
+//   * L2 eviction priority per load: Q tiles (read once) evict-first; K/V
+//     tiles by the caller's per-column hint (popular columns evict-last,
+//     columns used by one window evict-first).
 //   * Warp specialisation: warp 8 is the producer (ticket fetch, window
 //     metadata, block-column list read 32 at a time, TMA issue into a ring of
 //     STAGES K/V stages guarded by full/empty mbarriers); warps 0-7 consume.
-//     Consumer warp (hh, sp) owns head hh of the group and every SPLITS-th
-//     block of the window (SPLITS = 8 / HG); partial (m, l, O) of the splits
-//     are merged through shared memory at the end of the window.
+//     Consumer warp (hh, sp) owns head hh of the group and the blocks whose
+//     global issue index is sp mod SPLITS (SPLITS = 8 / HG), each split with
+//     its own sub-ring of stages; partial (m, l, O) of the splits are merged
+//     through shared memory at the end of the window.
 //   * Per block and head: S = Q K^T with mma.sync m16n8k16 (Q fragments stay
 //     in registers for the whole window), row max / sum with quad shuffles,
 //     exp2 on the MUFU, P packed to fp16 straight from the accumulator
@@ -46,11 +54,17 @@ constexpr int kFwdThreads = (kConsumerWarps + 1) * 32;
 constexpr int kSmemBudget = 227 * 1024;
 constexpr uint64_t kWaitTimeoutNs = 10ull * 1000 * 1000 * 1000;  // 10 s: far above any legal wait
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLazyLog2 = 8.0f;  // running-max slack before an O rescale (p <= 256)
 
 template <int D, int HG>
 struct FwdCfg {
     static constexpr int SPLITS = kConsumerWarps / HG;
-    static constexpr int HC = HG * D / 64;           // 128-byte rows per node in one tile
+    static constexpr int HC = HG * D / 64;           // 128-byte head-chunks per node in one tile
+    // A tile arrives as two TMA boxes of HA and HB head-chunks (HA odd,
+    // HB = 0 or 1), node-major in shared memory: see chunk_row().
+    static constexpr int HA = (HC % 2 == 0) ? HC - 1 : HC;
+    static constexpr int HB = HC - HA;
+    static constexpr int NBOX = HB ? 2 : 1;
     static constexpr int TILE = 16 * HG * D * 2;     // bytes of one Q, K or V tile
     static constexpr int SLOT_F = 16 * D + 64;       // floats per merge slot (O partial + m/l)
     static constexpr int MERGE = (SPLITS - 1) * HG * SLOT_F * 4;
@@ -58,7 +72,14 @@ struct FwdCfg {
     // stages) + 1 KB slack for aligning the dynamic shared memory base
     static constexpr int FIXED = 2 * TILE + MERGE + 1024 + 1024;
     static constexpr int STAGES_FIT = (kSmemBudget - FIXED) / (2 * TILE);
-    static constexpr int STAGES = STAGES_FIT > 32 ? 32 : STAGES_FIT;
+    // Each split owns a sub-ring of S_SUB stages: block g (global issue
+    // index) goes to split g % SPLITS, slot (g / SPLITS) % S_SUB of its
+    // sub-ring.  Every stage is then consumed by one split, strictly in
+    // order, so a waiter is never two phases ahead of a stage (the mbarrier
+    // parity would alias).
+    static constexpr int S_SUB = (STAGES_FIT > 32 ? 32 : STAGES_FIT) / SPLITS;
+    static constexpr int STAGES = S_SUB * SPLITS;
+    static_assert(S_SUB >= 2, "need at least two stages per split");
     static constexpr int Q_OFF = 0;
     static constexpr int KV_OFF = 2 * TILE;
     static constexpr int MERGE_OFF = KV_OFF + STAGES * 2 * TILE;
@@ -88,7 +109,7 @@ struct FwdParams {
     int q_windows;      // windows in the slab
     int q_rows;         // rows of the Q / O slab
     int tail;           // N % 16 (0: no masked column)
-    int tma3d;          // 1: one 3-D TMA load per tile; 0: HC 2-D loads
+    const uint8_t* hints;  // per block column L2 hint (1 keep, 2 stream, else normal) or null
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -102,21 +123,33 @@ __device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, const E
     return __all_sync(0xffffffffu, ok);
 }
 
-template <int HC>
-__device__ __forceinline__ void load_tile(const CUtensorMap* tm, uint32_t dst, uint32_t bar, int row, int z0,
-                                          int tma3d) {
-    if (tma3d) {
-        tma_load_3d(dst, tm, bar, 0, row, z0);
-    } else {
-#pragma unroll
-        for (int j = 0; j < HC; ++j) tma_load_2d(dst + j * 2048, tm, bar, (z0 + j) * 64, row);
-    }
+// Inline fast path: one try_wait per lane and a vote; the bounded slow path
+// only when the phase is not complete yet.
+__device__ __forceinline__ bool wait_fast(uint32_t bar, uint32_t parity, const ErrorSink& e, uint64_t tmo) {
+    const bool ready = mbar_try_wait(bar, parity);
+    if (__all_sync(0xffffffffu, ready)) return true;
+    return wait_warp(bar, parity, e, tmo);
+}
+
+// Tensor maps of Q, K and V: 3-D {64 elems, head-chunk, node} views with a
+// box of HA head-chunks (a) and one of a single head-chunk (b).
+struct FwdMaps {
+    CUtensorMap qa, qb, ka, kb, va, vb;
+};
+
+// Shared-memory row (128-byte unit) of head-chunk hc of node n in a tile.
+// Box a holds head-chunks [0, HA) node-major (row n*HA + hc), box b the last
+// one (row 16*HA + n).  HA is odd, so the 8 nodes an ldmatrix phase reads
+// from one head-chunk fall on 8 different 128-byte swizzle rows
+// ((n*HA + hc) mod 8 are distinct): conflict-free.
+template <int HA>
+__device__ __forceinline__ uint32_t chunk_row(int hc, int n) {
+    return hc < HA ? (uint32_t)(n * HA + hc) : (uint32_t)(16 * HA + n);
 }
 
 template <int D, int HG>
 __global__ void __launch_bounds__(kFwdThreads, 1)
-    k_fused3s(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-              const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
+    k_fused3s(const __grid_constant__ FwdMaps maps, const FwdParams p) {
     using C = FwdCfg<D, HG>;
     constexpr int S = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -135,6 +168,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     auto qempty = [&](uint32_t q) { return bar0 + 8u * (2 * S + 2 + q); };
     const uint32_t mfull = bar0 + 8u * (2 * S + 4);
     const uint32_t mempty = bar0 + 8u * (2 * S + 5);
+    // Block j of a window belongs to split j % SPLITS; a split's l-th block
+    // (counted over all its windows) uses slot l % S_SUB of its sub-ring, in
+    // phase l / S_SUB.
+    auto slot_of = [](uint32_t sp, uint32_t l) -> uint32_t { return sp * C::S_SUB + l % C::S_SUB; };
+    auto par_of = [](uint32_t l) -> uint32_t { return (l / C::S_SUB) & 1u; };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const ErrorSink err{&p.hdr->abort, &p.hdr->status};
@@ -156,13 +194,33 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------ producer --
+        // The whole warp runs this loop.  A block's K and V tiles are NBOX
+        // boxes each; lanes [0, NBOX) issue the K boxes and lanes
+        // [NBOX, 2*NBOX) the V boxes in one warp instruction (lanes
+        // [0, NBOX) also issue a window's Q boxes).
         if (lane == 0) {
-            tma_prefetch_desc(&tmQ);
-            tma_prefetch_desc(&tmK);
-            tma_prefetch_desc(&tmV);
+            tma_prefetch_desc(&maps.qa);
+            tma_prefetch_desc(&maps.qb);
+            tma_prefetch_desc(&maps.ka);
+            tma_prefetch_desc(&maps.kb);
+            tma_prefetch_desc(&maps.va);
+            tma_prefetch_desc(&maps.vb);
         }
+        const uint64_t pol_first = l2_policy_evict_first();
+        const uint64_t pol_normal = l2_policy_evict_normal();
+        const uint64_t pol_last = l2_policy_evict_last();
+        const int b_total = __ldg(p.offsets + p.nrw_total);
         const int total = p.num_items * p.groups;
-        uint32_t it = 0;  // K/V stages issued
+        const int bi = lane % C::NBOX;  // box of this lane: 0 = a (HA chunks), 1 = b (last chunk)
+        const bool vlane = lane >= C::NBOX;
+        const CUtensorMap* tkv = vlane ? (bi ? &maps.vb : &maps.va) : (bi ? &maps.kb : &maps.ka);
+        const CUtensorMap* tq = bi ? &maps.qb : &maps.qa;
+        const uint32_t box_off = bi ? (uint32_t)(C::HA * 2048) : 0u;  // 16 nodes x HA x 128 B
+        const int box_hc = bi ? C::HA : 0;
+        const uint32_t kv_half = vlane ? (uint32_t)C::TILE : 0u;
+        uint32_t cnt[C::SPLITS];  // blocks issued per split
+#pragma unroll
+        for (int t = 0; t < C::SPLITS; ++t) cnt[t] = 0;
         int k = 0;        // windows published
         bool aborted = false;
         int item = 0;
@@ -183,9 +241,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 }
                 b0 = __ldg(p.offsets + w);
                 b1 = __ldg(p.offsets + w + 1);
+                if (b0 < 0 || b1 < b0 || b1 > b_total) {
+                    if (lane == 0) raise_error(err, F3S_ERR_BAD_FORMAT);
+                    aborted = true;
+                    break;
+                }
             }
             const int q = k & 1;
-            if (!wait_warp(qempty(q), ((k >> 1) & 1) ^ 1, err, p.timeout_ns)) {
+            if (!wait_fast(qempty(q), ((k >> 1) & 1) ^ 1, err, p.timeout_ns)) {
                 aborted = true;
                 break;
             }
@@ -196,49 +259,70 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     mbar_arrive(qfull(q));
                 } else {
                     winfo[q] = make_int4(w, g, b0, b1);
-                    if (b1 > b0) {
+                    if (b1 > b0)
                         mbar_arrive_expect_tx(qfull(q), C::TILE);
-                        load_tile<C::HC>(&tmQ, q_s + q * C::TILE, qfull(q), 16 * (w - p.q_window_base), z0,
-                                         p.tma3d);
-                    } else {
+                    else
                         mbar_arrive(qfull(q));
-                    }
                 }
             }
             if (end) break;
+            __syncwarp();
+            if (b1 > b0 && lane < C::NBOX)
+                tma_load_3d_hint(q_s + q * C::TILE + box_off, tq, qfull(q), 0, z0 + box_hc,
+                                 16 * (w - p.q_window_base), pol_first);
             ++k;
-            for (int base = b0; base < b1 && !aborted; base += 32) {
+            int myc = lane < b1 - b0 ? __ldg(p.cols + b0 + lane) : 0;
+            for (int base = b0; base < b1; base += 32) {
                 const int n = min(32, b1 - base);
-                const int myc = lane < n ? __ldg(p.cols + base + lane) : 0;
-                if (__any_sync(0xffffffffu, myc < 0 || myc >= p.nrw_total)) {
+                // next chunk of the block list, in flight while this one issues
+                const int nbase = base + 32;
+                const int nc = nbase + lane < b1 ? __ldg(p.cols + nbase + lane) : 0;
+                if (__any_sync(0xffffffffu, lane < n && (myc < 0 || myc >= p.nrw_total))) {
                     if (lane == 0) raise_error(err, F3S_ERR_BAD_FORMAT);
                     aborted = true;
                     break;
                 }
+                const int myh = (p.hints != nullptr && lane < n) ? (int)__ldg(p.hints + myc) : 0;
                 for (int i = 0; i < n; ++i) {
                     const int c = __shfl_sync(0xffffffffu, myc, i);
-                    const uint32_t s = it % S;
-                    if (!wait_warp(empty(s), ((it / S) & 1) ^ 1, err, p.timeout_ns)) {
+                    const int h = __shfl_sync(0xffffffffu, myh, i);
+                    const int bsp = (base - b0 + i) % C::SPLITS;
+                    uint32_t l = 0;
+#pragma unroll
+                    for (int t = 0; t < C::SPLITS; ++t)
+                        if (t == bsp) l = cnt[t];
+                    const uint32_t s = slot_of(bsp, l);
+                    if (!wait_fast(empty(s), par_of(l) ^ 1u, err, p.timeout_ns)) {
                         aborted = true;
                         break;
                     }
                     if (lane == 0) {
                         stage_col[s] = c;
                         mbar_arrive_expect_tx(full(s), 2 * C::TILE);
-                        const uint32_t dst = kv_s + s * 2 * C::TILE;
-                        load_tile<C::HC>(&tmK, dst, full(s), 16 * c, z0, p.tma3d);
-                        load_tile<C::HC>(&tmV, dst + C::TILE, full(s), 16 * c, z0, p.tma3d);
                     }
-                    ++it;
+                    __syncwarp();
+                    if (lane < 2 * C::NBOX) {
+                        const uint64_t pol = h == 1 ? pol_last : (h == 2 ? pol_first : pol_normal);
+                        tma_load_3d_hint(kv_s + s * 2 * C::TILE + kv_half + box_off, tkv, full(s), 0,
+                                         z0 + box_hc, 16 * c, pol);
+                    }
+#pragma unroll
+                    for (int t = 0; t < C::SPLITS; ++t)
+                        if (t == bsp) cnt[t] = l + 1;
                 }
+                if (aborted) break;
+                myc = nc;
             }
             if (aborted) break;
             item = __shfl_sync(0xffffffffu, nxt, 0);
         }
         if (aborted && lane == 0) {
             // let this CTA's own bulk copies land before it exits
-            const uint32_t n = it < (uint32_t)S ? it : (uint32_t)S;
-            for (uint32_t j = it - n; j < it; ++j) mbar_drain(full(j % S), (j / S) & 1, 100000000ull);
+#pragma unroll
+            for (int t = 0; t < C::SPLITS; ++t) {
+                const uint32_t n = cnt[t] < (uint32_t)C::S_SUB ? cnt[t] : (uint32_t)C::S_SUB;
+                for (uint32_t l = cnt[t] - n; l < cnt[t]; ++l) mbar_drain(full(slot_of(t, l)), par_of(l), 100000000ull);
+            }
             for (int kk = k > 2 ? k - 2 : 0; kk < k; ++kk) mbar_drain(qfull(kk & 1), (kk >> 1) & 1, 100000000ull);
         }
         return;
@@ -254,7 +338,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int b_chk = (lane >> 3) & 1;
     constexpr int KS = D / 16;  // k-steps of QK^T, and 16-column pairs of PV
     constexpr int NT = D / 8;   // n-tiles of the O accumulator
-    uint32_t it = 0;
+    uint32_t mycnt = 0;  // blocks this warp's split has consumed, over all windows
     for (int k = 0;; ++k) {
         const int q = k & 1;
         if (!wait_warp(qfull(q), (k >> 1) & 1, err, p.timeout_ns)) return;
@@ -266,7 +350,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             const uint32_t qt = q_s + q * C::TILE;
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks) {
-                const uint32_t row = (hh * (D / 64) + ks / 4) * 16 + a_row;
+                const uint32_t row = chunk_row<C::HA>(hh * (D / 64) + ks / 4, a_row);
                 ldsm_x4(qt + swz128(row, (ks & 3) * 2 + a_chk), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
             }
         }
@@ -276,82 +360,129 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         float o[NT][4];
 #pragma unroll
         for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-        float m0 = -1e30f, m1 = -1e30f, l0 = 0.f, l1 = 0.f;  // m in log2 units
+        // Running row max m (log2 units) and sum l.  The max moves lazily:
+        // only when a row's block max exceeds it by more than kLazyLog2, so
+        // most blocks skip the O rescale; p = 2^(s*log2e - m) <= 2^kLazyLog2
+        // stays well inside fp16, and O / l is unchanged because both use
+        // the same m.
+        float m0 = -1e30f, m1 = -1e30f, l0 = 0.f, l1 = 0.f;
         bool ok = true;
-        for (int j = sp; j < nb; j += C::SPLITS) {
-            const uint32_t idx = it + (uint32_t)j;
-            const uint32_t s = idx % S;
-            if (!wait_warp(full(s), (idx / S) & 1, err, p.timeout_ns)) {
-                ok = false;
-                break;
-            }
-            const uint32_t kt = kv_s + s * 2 * C::TILE;
-            const uint32_t vt = kt + C::TILE;
-            float sc[2][4];
+        auto qk_tile = [&](uint32_t kt, float (&sc)[2][4]) {
 #pragma unroll
             for (int i = 0; i < 4; ++i) sc[0][i] = sc[1][i] = 0.f;
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks) {
-                const uint32_t row = (hh * (D / 64) + ks / 4) * 16 + b_row;
+                const uint32_t row = chunk_row<C::HA>(hh * (D / 64) + ks / 4, b_row);
                 uint32_t k0, k1, k2, k3;
                 ldsm_x4(kt + swz128(row, (ks & 3) * 2 + b_chk), k0, k1, k2, k3);
                 mma_16816(sc[0], qa[ks], k0, k1);
                 mma_16816(sc[1], qa[ks], k2, k3);
             }
-            if (p.tail != 0 && stage_col[s] == p.nrw_total - 1) {
+        };
+        auto mask_tail = [&](float (&sc)[2][4], int col) {
+            if (col == p.nrw_total - 1) {
 #pragma unroll
                 for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
                     for (int i = 0; i < 4; ++i)
                         if (nt * 8 + 2 * t4 + (i & 1) >= p.tail) sc[nt][i] = -INFINITY;
             }
-            float mx0 = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
-            float mx1 = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-            const float mn0 = fmaxf(m0, mx0 * kLog2e);
-            const float mn1 = fmaxf(m1, mx1 * kLog2e);
-            const float c0 = fast_exp2(m0 - mn0);
-            const float c1 = fast_exp2(m1 - mn1);
-            m0 = mn0;
-            m1 = mn1;
-            float pr[2][4];
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-                pr[nt][0] = fast_exp2(fmaf(sc[nt][0], kLog2e, -mn0));
-                pr[nt][1] = fast_exp2(fmaf(sc[nt][1], kLog2e, -mn0));
-                pr[nt][2] = fast_exp2(fmaf(sc[nt][2], kLog2e, -mn1));
-                pr[nt][3] = fast_exp2(fmaf(sc[nt][3], kLog2e, -mn1));
-            }
-            l0 = fmaf(l0, c0, (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]));
-            l1 = fmaf(l1, c1, (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]));
-#pragma unroll
-            for (int jn = 0; jn < NT; ++jn) {
-                o[jn][0] *= c0;
-                o[jn][1] *= c0;
-                o[jn][2] *= c1;
-                o[jn][3] *= c1;
-            }
-            uint32_t pa[4];
-            pa[0] = pack_half2(pr[0][0], pr[0][1]);
-            pa[1] = pack_half2(pr[0][2], pr[0][3]);
-            pa[2] = pack_half2(pr[1][0], pr[1][1]);
-            pa[3] = pack_half2(pr[1][2], pr[1][3]);
+        };
+        auto pv_tile = [&](uint32_t vt, const uint32_t (&pa)[4]) {
 #pragma unroll
             for (int jj = 0; jj < KS; ++jj) {
-                const uint32_t row = (hh * (D / 64) + jj / 4) * 16 + a_row;
+                const uint32_t row = chunk_row<C::HA>(hh * (D / 64) + jj / 4, a_row);
                 uint32_t v0, v1, v2, v3;
                 ldsm_x4_t(vt + swz128(row, (jj & 3) * 2 + a_chk), v0, v1, v2, v3);
                 mma_16816(o[2 * jj], pa, v0, v1);
                 mma_16816(o[2 * jj + 1], pa, v2, v3);
             }
+        };
+        // Two blocks per step (this warp's j-th and (j+SPLITS)-th): their
+        // QK^T, exp and PV chains interleave, and one max update / rescale
+        // covers 32 columns.
+        // This split's blocks j = sp, sp + SPLITS, ... of the window are its
+        // local blocks mycnt, mycnt + 1, ...
+        // (d = 128 takes one block per step: its 64-register O accumulator
+        // leaves no room for a second block's scores under the 168-register
+        // budget of a 9-warp CTA)
+        constexpr int PAIR = D == 64 ? 2 : 1;
+        for (int j = sp; j < nb; j += PAIR * C::SPLITS) {
+            const bool two = PAIR == 2 && j + C::SPLITS < nb;  // warp-uniform
+            const uint32_t lc0 = mycnt + (uint32_t)(j - sp) / C::SPLITS, lc1 = lc0 + 1;
+            const uint32_t s0 = slot_of(sp, lc0), s1 = slot_of(sp, lc1);
+            float sc[2][2][4];
+            if (!wait_fast(full(s0), par_of(lc0), err, p.timeout_ns)) {
+                ok = false;
+                break;
+            }
+            qk_tile(kv_s + s0 * 2 * C::TILE, sc[0]);
+            if (two) {
+                if (!wait_fast(full(s1), par_of(lc1), err, p.timeout_ns)) {
+                    ok = false;
+                    break;
+                }
+                qk_tile(kv_s + s1 * 2 * C::TILE, sc[1]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) sc[1][0][i] = sc[1][1][i] = -INFINITY;
+            }
+            if (p.tail != 0) {
+                mask_tail(sc[0], stage_col[s0]);
+                if (two) mask_tail(sc[1], stage_col[s1]);
+            }
+            float mx0 = fmaxf(fmaxf(fmaxf(sc[0][0][0], sc[0][0][1]), fmaxf(sc[0][1][0], sc[0][1][1])),
+                              fmaxf(fmaxf(sc[1][0][0], sc[1][0][1]), fmaxf(sc[1][1][0], sc[1][1][1])));
+            float mx1 = fmaxf(fmaxf(fmaxf(sc[0][0][2], sc[0][0][3]), fmaxf(sc[0][1][2], sc[0][1][3])),
+                              fmaxf(fmaxf(sc[1][0][2], sc[1][0][3]), fmaxf(sc[1][1][2], sc[1][1][3])));
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2)) * kLog2e;
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2)) * kLog2e;
+            const bool up0 = mx0 > m0 + kLazyLog2, up1 = mx1 > m1 + kLazyLog2;
+            if (__any_sync(0xffffffffu, up0 || up1)) {
+                const float mn0 = up0 ? mx0 : m0, mn1 = up1 ? mx1 : m1;
+                const float c0 = fast_exp2(m0 - mn0), c1 = fast_exp2(m1 - mn1);
+                l0 *= c0;
+                l1 *= c1;
+#pragma unroll
+                for (int jn = 0; jn < NT; ++jn) {
+                    o[jn][0] *= c0;
+                    o[jn][1] *= c0;
+                    o[jn][2] *= c1;
+                    o[jn][3] *= c1;
+                }
+                m0 = mn0;
+                m1 = mn1;
+            }
+            uint32_t pa[2][4];
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+                float pr[2][4];
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                    pr[nt][0] = fast_exp2(fmaf(sc[b][nt][0], kLog2e, -m0));
+                    pr[nt][1] = fast_exp2(fmaf(sc[b][nt][1], kLog2e, -m0));
+                    pr[nt][2] = fast_exp2(fmaf(sc[b][nt][2], kLog2e, -m1));
+                    pr[nt][3] = fast_exp2(fmaf(sc[b][nt][3], kLog2e, -m1));
+                }
+                l0 += (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
+                l1 += (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
+                pa[b][0] = pack_half2(pr[0][0], pr[0][1]);
+                pa[b][1] = pack_half2(pr[0][2], pr[0][3]);
+                pa[b][2] = pack_half2(pr[1][0], pr[1][1]);
+                pa[b][3] = pack_half2(pr[1][2], pr[1][3]);
+            }
+            pv_tile(kv_s + s0 * 2 * C::TILE + C::TILE, pa[0]);
+            if (two) pv_tile(kv_s + s1 * 2 * C::TILE + C::TILE, pa[1]);
             __syncwarp();
-            if (lane == 0) mbar_arrive(empty(s));
+            if (lane == 0) {
+                mbar_arrive(empty(s0));
+                if (two) mbar_arrive(empty(s1));
+            }
         }
         if (!ok) return;
-        it += (uint32_t)nb;
+        mycnt += nb > sp ? (uint32_t)(nb - 1 - sp) / C::SPLITS + 1 : 0u;
         l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
         l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
         l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
@@ -430,33 +561,23 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// Tensor map over fp16 [rows, heads, head_dim] whose box is one node-tile of
-// `box_hc` 128-byte head-chunks: 3-D {64, rows, heads*head_dim/64} with the
-// head-chunk stride (128 B) below the node stride, or the 2-D fallback
-// {heads*head_dim, rows} with a {64, 16} box.
-static bool encode_map(CUtensorMap* m, const void* base, int rows, int heads, int head_dim, int box_hc,
-                       bool three_d) {
+// Tensor map over fp16 [rows, heads, head_dim] viewed as the 3-D tensor
+// {64 elems, heads*head_dim/64 head-chunks, rows}: strides 128 B and
+// heads*head_dim*2 B, each the previous dimension's full extent, as the
+// driver documents.  The box is {64, box_chunks, 16}: box_chunks head-chunks
+// of 16 consecutive nodes.  (A map whose head-chunk stride lies below the
+// node stride is accepted by the encoder but is outside the documented
+// contract -- and faulted here on a 17 GB tensor -- so it is never built.)
+static bool encode_map(CUtensorMap* m, const void* base, int rows, int heads, int head_dim, int box_chunks) {
     auto enc = tensor_map_encoder();
     if (!enc) return false;
-    const cuuint64_t row_bytes = (cuuint64_t)heads * head_dim * 2;
-    CUresult r;
-    if (three_d) {
-        cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)heads * head_dim / 64};
-        cuuint64_t strides[2] = {row_bytes, 128};
-        cuuint32_t box[3] = {64, 16, (cuuint32_t)box_hc};
-        cuuint32_t es[3] = {1, 1, 1};
-        r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    } else {
-        cuuint64_t dims[2] = {(cuuint64_t)heads * head_dim, (cuuint64_t)rows};
-        cuuint64_t strides[1] = {row_bytes};
-        cuuint32_t box[2] = {64, 16};
-        cuuint32_t es[2] = {1, 1};
-        r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    }
+    cuuint64_t dims[3] = {64, (cuuint64_t)heads * head_dim / 64, (cuuint64_t)rows};
+    cuuint64_t strides[2] = {128, (cuuint64_t)heads * head_dim * 2};
+    cuuint32_t box[3] = {64, (cuuint32_t)box_chunks, 16};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
@@ -473,30 +594,23 @@ static int ensure_smem_attr() {
     return F3S_SUCCESS;
 }
 
-static int g_tma_mode = -1;  // -1 unknown, 1 three-d maps accepted, 0 two-d fallback
-
 template <int D, int HG>
 static int launch_variant(const void* Q, const void* K, const void* V, FwdParams prm, int q_rows,
                           cudaStream_t stream) {
     using C = FwdCfg<D, HG>;
     int rc = ensure_smem_attr<D, HG>();
     if (rc != F3S_SUCCESS) return rc;
-    CUtensorMap mq, mk, mv;
-    bool three = g_tma_mode != 0;
-    bool okq = encode_map(&mq, Q, q_rows, prm.heads, D, C::HC, three);
-    if (!okq && three) {  // driver refused the 3-D form: fall back for good
-        three = false;
-        g_tma_mode = 0;
-        okq = encode_map(&mq, Q, q_rows, prm.heads, D, C::HC, false);
-    }
-    if (!okq || !encode_map(&mk, K, prm.num_nodes, prm.heads, D, C::HC, three) ||
-        !encode_map(&mv, V, prm.num_nodes, prm.heads, D, C::HC, three))
+    FwdMaps maps;
+    const int hb = C::HB ? C::HB : 1;  // box b is unused when HB == 0; encode a valid map anyway
+    if (!encode_map(&maps.qa, Q, q_rows, prm.heads, D, C::HA) || !encode_map(&maps.qb, Q, q_rows, prm.heads, D, hb) ||
+        !encode_map(&maps.ka, K, prm.num_nodes, prm.heads, D, C::HA) ||
+        !encode_map(&maps.kb, K, prm.num_nodes, prm.heads, D, hb) ||
+        !encode_map(&maps.va, V, prm.num_nodes, prm.heads, D, C::HA) ||
+        !encode_map(&maps.vb, V, prm.num_nodes, prm.heads, D, hb))
         return F3S_ERR_INVALID_VALUE;
-    if (three) g_tma_mode = 1;
-    prm.tma3d = three ? 1 : 0;
     const int items = prm.num_items * prm.groups;
     const int grid = std::max(1, std::min(items, num_sms_of_current_device()));
-    k_fused3s<D, HG><<<grid, kFwdThreads, C::SMEM, stream>>>(mq, mk, mv, prm);
+    k_fused3s<D, HG><<<grid, kFwdThreads, C::SMEM, stream>>>(maps, prm);
     F3S_LAUNCH_CHECK();
     return F3S_SUCCESS;
 }
@@ -511,8 +625,9 @@ static int pick_head_group(int heads, int head_dim) {
 }
 
 int forward_impl(const void* Q, const void* K, const void* V, float* O, const int* offsets, const int* cols,
-                 const int* order, int num_items, int num_nodes, int heads, int head_dim, int q_window_base,
-                 int q_rows, void* ws, size_t ws_bytes, cudaStream_t stream, uint64_t timeout_ns) {
+                 const int* order, const uint8_t* col_hints, int num_items, int num_nodes, int heads, int head_dim,
+                 int q_window_base, int q_rows, void* ws, size_t ws_bytes, cudaStream_t stream,
+                 uint64_t timeout_ns) {
     if (num_items < 0 || num_nodes < 0 || heads <= 0 || q_window_base < 0 || q_rows < 0)
         return F3S_ERR_INVALID_VALUE;
     if (head_dim != 64 && head_dim != 128) return F3S_ERR_UNSUPPORTED;
@@ -529,6 +644,7 @@ int forward_impl(const void* Q, const void* K, const void* V, float* O, const in
     prm.offsets = offsets;
     prm.cols = cols;
     prm.order = order;
+    prm.hints = col_hints;
     prm.hdr = static_cast<WsHeader*>(ws);
     prm.timeout_ns = timeout_ns;
     prm.num_items = num_items;
@@ -592,11 +708,11 @@ extern "C" {
 size_t f3s_forward_workspace_size(void) { return f3s::kWsHeaderBytes; }
 
 int f3s_forward(const void* d_Q, const void* d_K, const void* d_V, float* d_O, const int32_t* d_window_offsets,
-                const int32_t* d_block_cols, const int32_t* d_order, int32_t num_items, int32_t num_nodes,
-                int32_t heads, int32_t head_dim, int32_t q_window_base, int32_t q_rows, void* d_workspace,
-                size_t workspace_bytes, f3s_stream_t stream) {
-    return f3s::forward_impl(d_Q, d_K, d_V, d_O, d_window_offsets, d_block_cols, d_order, num_items, num_nodes,
-                             heads, head_dim, q_window_base, q_rows, d_workspace, workspace_bytes,
+                const int32_t* d_block_cols, const int32_t* d_order, const uint8_t* d_col_hints, int32_t num_items,
+                int32_t num_nodes, int32_t heads, int32_t head_dim, int32_t q_window_base, int32_t q_rows,
+                void* d_workspace, size_t workspace_bytes, f3s_stream_t stream) {
+    return f3s::forward_impl(d_Q, d_K, d_V, d_O, d_window_offsets, d_block_cols, d_order, d_col_hints, num_items,
+                             num_nodes, heads, head_dim, q_window_base, q_rows, d_workspace, workspace_bytes,
                              (cudaStream_t)stream, f3s::kWaitTimeoutNs);
 }
 

@@ -151,6 +151,8 @@ int f3s_window_order(const int32_t* d_window_offsets, int32_t num_row_windows, i
  *   d_window_offsets / d_block_cols: the converter's output for all windows
  *   d_order  int32[num_items] window ids to compute (any subset, any order;
  *            each must lie in [q_window_base, q_window_base + ceil(q_rows/16)))
+ *   d_col_hints optional uint8[nrw] per block column L2 eviction hint from
+ *            f3s_column_hints (NULL: no hint); affects speed only.
  *   q_window_base / q_rows: 0 / num_nodes on one GPU; a rank's slab when the
  *            windows are sharded across GPUs.
  * head_dim in {64, 128}; heads >= 1.  No padding of any tensor is needed:
@@ -160,9 +162,25 @@ int f3s_window_order(const int32_t* d_window_offsets, int32_t num_row_windows, i
 size_t f3s_forward_workspace_size(void);
 int f3s_forward(const void* d_Q, const void* d_K, const void* d_V, float* d_O,
                 const int32_t* d_window_offsets, const int32_t* d_block_cols, const int32_t* d_order,
-                int32_t num_items, int32_t num_nodes, int32_t heads, int32_t head_dim,
-                int32_t q_window_base, int32_t q_rows, void* d_workspace, size_t workspace_bytes,
-                f3s_stream_t stream);
+                const uint8_t* d_col_hints, int32_t num_items, int32_t num_nodes, int32_t heads,
+                int32_t head_dim, int32_t q_window_base, int32_t q_rows, void* d_workspace,
+                size_t workspace_bytes, f3s_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Per block column L2 eviction hints for f3s_forward (no reference
+ * counterpart: a speed hint computed once per graph and window set).
+ *
+ * Counts, for the windows listed in d_order[0 .. num_items), how many of
+ * them reference each block column; the most popular columns whose K/V
+ * bytes (bytes_per_column = 16 * heads * head_dim * 2 * 2) fit in
+ * l2_budget_bytes get hint 1 (keep: evict-last), columns referenced once get
+ * hint 2 (stream: evict-first), the rest 0.  d_col_hints: uint8[nrw].
+ * ---------------------------------------------------------------------- */
+size_t f3s_column_hints_workspace_size(int32_t num_row_windows);
+int f3s_column_hints(const int32_t* d_window_offsets, const int32_t* d_block_cols, const int32_t* d_order,
+                     int32_t num_items, int32_t num_row_windows, int64_t bytes_per_column,
+                     int64_t l2_budget_bytes, uint8_t* d_col_hints, void* d_workspace,
+                     size_t workspace_bytes, f3s_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Drop-in launch with the reference kernel's exact argument list

@@ -208,3 +208,48 @@ def test_forward_graph_without_edges(lib):
 def test_float2half_matches_torch(lib):
     x = torch.randn(1 << 20, device="cuda") * 100
     assert torch.equal(F.float2half(x), x.half())
+
+
+def test_column_hints_only_change_speed(lib):
+    """L2 hints are valid (0/1/2), mark single-use columns as streamed, and
+    leave the output bit-identical."""
+    g = G.rmat_graph(14, 16, device="cuda", name="rmat14")
+    q, k, v = features_np(g.num_nodes, 8, 64, "normal")
+    fmt = F.convert_csr_to_block_sparse(g.num_nodes, g.row_ptr, g.col_ind)
+    Q, K, V = to_gpu(q, k, v)
+    hints = F.column_hints(fmt, 8, 64, l2_fraction=0.001)
+    h = hints.cpu().numpy()
+    assert set(np.unique(h)) <= {0, 1, 2}
+    off, cols = fmt.to_host()
+    pop = np.bincount(cols, minlength=fmt.num_row_windows)
+    assert np.all(h[pop == 1] == 2)
+    if (h == 1).any():
+        assert pop[h == 1].min() >= pop[h == 0].max(initial=0)
+    a = F.fused3s_forward(Q, K, V, fmt, check_status=True).cpu()
+    b = F.fused3s_forward(Q, K, V, fmt, col_hints=hints, check_status=True).cpu()
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("heads,head_dim", [(1, 64), (2, 128), (4, 128)])
+def test_forward_heavy_windows_split_heads(lib, heads, head_dim):
+    """Consumer warps that split a window's blocks (heads < 8) on windows of
+    tens of thousands of blocks: every split must see its own blocks in
+    order.  A few hub rows connect to every node."""
+    rng = np.random.default_rng(heads)
+    n = 1 << 19
+    hubs = np.arange(0, 48)  # windows 0-2: hubs linked to every 16th node
+    s = np.r_[np.repeat(hubs, n // 16), rng.integers(0, n, 4 * n)]
+    d = np.r_[np.tile(np.arange(0, n, 16), len(hubs)) + rng.integers(0, 16, len(hubs) * (n // 16)),
+              rng.integers(0, n, 4 * n)]
+    gr = G.csr_from_edges(n, s, d)
+    q, k, v = features_np(n, heads, head_dim, "normal", seed=heads)
+    fmt, o = forward_np(n, gr.row_ptr, gr.col_ind, q, k, v)
+    off, cols = fmt.to_host()
+    assert np.diff(off).max() >= n // 16
+    wins = np.r_[np.arange(3), np.random.default_rng(0).choice(fmt.num_row_windows, 64, replace=False)]
+    ref = oracle.block_attention(n, q.astype(np.float32), k.astype(np.float32), v.astype(np.float32), off, cols,
+                                 windows=np.unique(wins).astype(np.int32), threads=16)
+    rows = (np.unique(wins)[:, None] * 16 + np.arange(16)).reshape(-1)
+    assert_parity(o[rows], ref[rows], f"heavy H={heads} d={head_dim}")
+    again = F.fused3s_forward(*to_gpu(q, k, v), fmt, check_status=True).cpu().numpy()
+    assert np.array_equal(again, o)
