@@ -258,6 +258,9 @@ def run_ours(args):
 
     rank, world, local = dist_env()
     if world > 1:
+        # keep stdout to the one JSON line: no NCCL version banner
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
@@ -305,11 +308,23 @@ def run_ours(args):
         torch.cuda.synchronize()
         hints_ms = (time.perf_counter() - t0) * 1e3
     hints_ptr = hints.data_ptr() if hints is not None else None
+    # work plan: heavy windows cut into pieces (computed once per graph and rank)
+    plan = None
+    plan_ms = None
+    if args.split != "off":
+        my_blocks_total = int((fmt.window_offsets[1:] - fmt.window_offsets[:-1])[lo:hi].sum().item())
+        T = F.auto_piece_blocks(my_blocks_total, dev) if args.split == "auto" else int(args.split)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        plan = F.make_plan(fmt, H, d, order=my_order, max_blocks=T)
+        torch.cuda.synchronize()
+        plan_ms = (time.perf_counter() - t0) * 1e3
+    plan_ptr = plan.buffer.data_ptr() if plan is not None else None
 
     def step():
         st = lib.f3s_forward(Q.data_ptr(), Kf.data_ptr(), Vf.data_ptr(), O.data_ptr(),
                              fmt.window_offsets.data_ptr(), fmt.cols_ptr, my_order.data_ptr(), hints_ptr,
-                             n_items, N, H, d, lo, r1 - r0, ws.data_ptr(), ws.numel(), sptr)
+                             plan_ptr, n_items, N, H, d, lo, r1 - r0, ws.data_ptr(), ws.numel(), sptr)
         if st != 0:
             raise _lib.Fused3SError(st, "f3s_forward")
 
@@ -364,7 +379,8 @@ def run_ours(args):
             dQ.copy_(hQ, non_blocking=True)
             dK.copy_(hK, non_blocking=True)
             dV.copy_(hV, non_blocking=True)
-            F.fused3s_forward(dQ, dK, dV, fmt, order=my_order, out=O, q_window_base=lo, col_hints=hints)
+            F.fused3s_forward(dQ, dK, dV, fmt, order=my_order, out=O, q_window_base=lo, col_hints=hints,
+                              plan=plan)
             hO.copy_(O, non_blocking=True)
 
         for _ in range(max(1, args.warmup // 2)):
@@ -437,7 +453,8 @@ def run_ours(args):
                        "l2": "inputs larger than L2" if (Kf.numel() + Vf.numel()) * 2 > 126e6 else
                              "inputs fit in L2 (no flush)",
                        "convert_ms": convert_ms, "order_ms": order_ms, "l2_hints": args.l2_hints,
-                       "hints_ms": hints_ms},
+                       "hints_ms": hints_ms, "split": args.split,
+                       "piece_blocks": plan.max_blocks if plan is not None else None, "plan_ms": plan_ms},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "traffic": traffic, "peak_kind": peak_kind,
                          "alg_bytes_per_launch": bytes_launch, "kernel_ms": kern_ms,
@@ -465,6 +482,8 @@ def main(argv=None):
     ap.add_argument("--config", default="c4", choices=["c1", "c2", "c3", "c4", "c5", "c4s"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gather", action="store_true", help="also time the NCCL all-gather of O (N > 1)")
+    ap.add_argument("--split", default="auto",
+                    help="cut windows above this many blocks into pieces: auto, off or a number")
     ap.add_argument("--l2-hints", default="on", choices=["on", "off"],
                     help="per block column L2 eviction hints (computed once per graph)")
     ap.add_argument("--no-e2e", action="store_true")

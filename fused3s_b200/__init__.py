@@ -8,7 +8,9 @@ below.
 from .api import (
     BlockSparseFormat,
     GraphData,
+    ForwardPlan,
     Fused3SError,
+    auto_piece_blocks,
     column_hints,
     convert_csr_to_block_sparse,
     f3s_1tb1rw_kernel,
@@ -17,16 +19,20 @@ from .api import (
     fused3s_forward,
     generate_balanced_window_order,
     load_csr_graph,
+    make_plan,
     workspace_status,
 )
 
 __all__ = [
     "BlockSparseFormat",
     "GraphData",
+    "ForwardPlan",
     "Fused3SError",
+    "auto_piece_blocks",
     "column_hints",
     "convert_csr_to_block_sparse",
     "f3s_1tb1rw_kernel",
+    "make_plan",
     "float2half",
     "forward_workspace",
     "fused3s_forward",

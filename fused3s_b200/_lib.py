@@ -40,8 +40,10 @@ SIGNATURES = {
     "f3s_window_order_workspace_size": (_SZ, [_I32]),
     "f3s_window_order": (ctypes.c_int, [_P, _I32, _P, _P, _SZ, _P]),
     "f3s_forward_workspace_size": (_SZ, []),
-    "f3s_forward": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _SZ,
-                                   _P]),
+    "f3s_forward": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P,
+                                   _SZ, _P]),
+    "f3s_plan_size": (_SZ, [_I32, _I64, _I32, _I32, _I32]),
+    "f3s_make_plan": (ctypes.c_int, [_P, _P, _I32, _I64, _I32, _I32, _I32, _P, _SZ, _P]),
     "f3s_column_hints_workspace_size": (_SZ, [_I32]),
     "f3s_column_hints": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I64, _I64, _P, _P, _SZ, _P]),
     "f3s_1tb1rw_launch": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _P]),

@@ -220,10 +220,53 @@ def column_hints(fmt: BlockSparseFormat, heads: int, head_dim: int, order: Optio
     return hints[:nrw]
 
 
+@dataclasses.dataclass
+class ForwardPlan:
+    """Device-resident work plan (f3s_make_plan): the listed windows in
+    order, heavy ones cut into pieces of at most `max_blocks` blocks."""
+    buffer: torch.Tensor
+    heads: int
+    head_dim: int
+    max_blocks: int
+
+
+def auto_piece_blocks(num_blocks: int, device=None) -> int:
+    """Piece size: a quarter of one SM's share of the blocks (so no single
+    window can hold one SM much past the others), never below 1024 blocks
+    (so the partial write stays a small overhead)."""
+    device = _default_device(device)
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    return max(1024, -(-int(num_blocks) // (4 * sms)))
+
+
+def make_plan(fmt: BlockSparseFormat, heads: int, head_dim: int, order: Optional[torch.Tensor] = None,
+              max_blocks: Optional[int] = None) -> ForwardPlan:
+    """Plan for fused3s_forward over the windows in `order` (default: the
+    balanced order of all windows)."""
+    lib = _lib.load()
+    device = fmt.window_offsets.device
+    if order is None:
+        order = generate_balanced_window_order(fmt)
+    order = order.to(device=device, dtype=torch.int32).contiguous()
+    n = int(order.numel())
+    nb = max(fmt.num_blocks, 1)
+    if max_blocks is None:
+        max_blocks = auto_piece_blocks(nb, device)
+    size = lib.f3s_plan_size(n, nb, int(max_blocks), heads, head_dim)
+    if size == 0:
+        raise ValueError("unsupported plan parameters")
+    buf = torch.empty(size, dtype=torch.uint8, device=device)
+    with torch.cuda.device(device):
+        st = lib.f3s_make_plan(_ptr(fmt.window_offsets), _ptr(order), n, nb, int(max_blocks), heads, head_dim,
+                               _ptr(buf), size, _stream_ptr(device))
+    check(st, "f3s_make_plan")
+    return ForwardPlan(buf, heads, head_dim, int(max_blocks))
+
+
 def fused3s_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: BlockSparseFormat,
                     order: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
                     q_window_base: int = 0, check_status: bool = False,
-                    col_hints: Optional[torch.Tensor] = None) -> torch.Tensor:
+                    col_hints: Optional[torch.Tensor] = None, plan: Optional[ForwardPlan] = None) -> torch.Tensor:
     """O = block-sparse softmax(Q K^T) V, fused (the fused3s_v2 path).
 
     Q: fp16 [q_rows, H, d] (or [q_rows, d] for one head) holding rows
@@ -232,7 +275,11 @@ def fused3s_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: Bloc
        the balanced order).  Returns fp32 O shaped like Q; rows of the listed
        windows are written in full (zeros for windows with no block).
     check_status: synchronise and raise if a kernel recorded an error.
-    col_hints: optional uint8[nrw] from column_hints() (speed only)."""
+    col_hints: optional uint8[nrw] from column_hints() (speed only).
+    plan: optional ForwardPlan from make_plan(); it then lists the windows
+       (order is ignored) and heavy windows run as several pieces."""
+    if plan is not None and (plan.heads, plan.head_dim) != (_as_nhd(Q).shape[1], _as_nhd(Q).shape[2]):
+        raise ValueError("plan was made for other heads / head_dim")
     if col_hints is not None and (col_hints.dtype != torch.uint8 or col_hints.numel() < fmt.num_row_windows):
         raise ValueError("col_hints must be uint8 with one entry per row window")
     lib = _lib.load()
@@ -245,7 +292,9 @@ def fused3s_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: Bloc
     if num_nodes != fmt.num_nodes:
         raise ValueError("K/V rows must equal the graph's num_nodes")
     device = Q.device
-    if order is None:
+    if plan is not None:
+        order = torch.zeros(1, dtype=torch.int32, device=device)  # unused: the plan lists the windows
+    elif order is None:
         if q_window_base == 0 and q_rows == num_nodes:
             order = generate_balanced_window_order(fmt)
         else:
@@ -259,7 +308,8 @@ def fused3s_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: Bloc
     ws = _WS.get(device, "forward", lib.f3s_forward_workspace_size())
     with torch.cuda.device(device):
         st = lib.f3s_forward(_ptr(Q), _ptr(K), _ptr(V), _ptr(out), _ptr(fmt.window_offsets),
-                             fmt.cols_ptr, _ptr(order), _ptr(col_hints), int(order.numel()), num_nodes, heads,
+                             fmt.cols_ptr, _ptr(order), _ptr(col_hints), None if plan is None else _ptr(plan.buffer),
+                             int(order.numel()), num_nodes, heads,
                              head_dim, q_window_base, q_rows, _ptr(ws), ws.numel(), _stream_ptr(device))
         check(st, "f3s_forward")
         if check_status:

@@ -72,11 +72,11 @@ struct FwdCfg {
     // stages) + 1 KB slack for aligning the dynamic shared memory base
     static constexpr int FIXED = 2 * TILE + MERGE + 1024 + 1024;
     static constexpr int STAGES_FIT = (kSmemBudget - FIXED) / (2 * TILE);
-    // Each split owns a sub-ring of S_SUB stages: block g (global issue
-    // index) goes to split g % SPLITS, slot (g / SPLITS) % S_SUB of its
-    // sub-ring.  Every stage is then consumed by one split, strictly in
-    // order, so a waiter is never two phases ahead of a stage (the mbarrier
-    // parity would alias).
+    // Each split owns a sub-ring of S_SUB stages: block j of a window goes to
+    // split j % SPLITS, and a split's l-th block (counted over its windows)
+    // to slot l % S_SUB of its sub-ring.  Every stage is then consumed by one
+    // split, strictly in order, so a waiter is never two phases ahead of a
+    // stage (the mbarrier parity would alias).
     static constexpr int S_SUB = (STAGES_FIT > 32 ? 32 : STAGES_FIT) / SPLITS;
     static constexpr int STAGES = S_SUB * SPLITS;
     static_assert(S_SUB >= 2, "need at least two stages per split");
@@ -87,17 +87,39 @@ struct FwdCfg {
     static constexpr int NBARS = 2 * STAGES + 6;
     static constexpr int META_OFF = BAR_OFF + NBARS * 8;
     static constexpr int WINFO_OFF = (META_OFF + STAGES * 4 + 15) / 16 * 16;
-    static constexpr int SMEM = WINFO_OFF + 2 * 16 + 1024;  // + slack to align the base to 1 KB
+    static constexpr int SMEM = WINFO_OFF + 4 * 16 + 1024;  // + slack to align the base to 1 KB
     static_assert(STAGES >= 2, "need at least two K/V stages");
     static_assert(SMEM <= kSmemBudget, "shared memory budget");
     static_assert(D % 64 == 0, "head_dim must be a multiple of 64");
 };
+
+// ---------------------------------------------------------------- plans --
+// A plan cuts every window with more than T active blocks into pieces of at
+// most T consecutive blocks so that one heavy window spreads over many SMs.
+// Each piece is a work item; a piece of a split window writes its partial
+// (running max m, sum l, unnormalised O) for its 16 rows and HG heads into
+// the plan's scratch, and k_merge_pieces combines the pieces of each window
+// in piece order (deterministic) and writes O.
+struct PlanHeader {
+    int num_pieces;        // work items (pieces) in the plan
+    int num_split;         // windows that were split
+    int num_split_pieces;  // pieces of split windows (partial slots used)
+    int max_pieces, max_split, max_split_pieces;
+    int max_blocks;        // T
+    int heads, head_dim, groups, hg;
+    int status;            // 0, or an f3s_status if the plan overflowed
+    long long splits_off;  // byte offsets of the sections; pieces follow the header
+    long long partials_off;
+    int pad[48];
+};
+static_assert(sizeof(PlanHeader) == 256, "plan header is 256 bytes");
 
 struct FwdParams {
     float* O;
     const int* offsets;
     const int* cols;
     const int* order;
+    PlanHeader* plan;          // plan (device), or null: one work item per entry of `order`
     WsHeader* hdr;
     uint64_t timeout_ns;
     int num_items;      // entries of `order`
@@ -210,7 +232,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const uint64_t pol_normal = l2_policy_evict_normal();
         const uint64_t pol_last = l2_policy_evict_last();
         const int b_total = __ldg(p.offsets + p.nrw_total);
-        const int total = p.num_items * p.groups;
+        int n_units = p.num_items;
+        const int4* pieces = nullptr;  // plan pieces (w, b0, b1, partial slot or -1)
+        if (p.plan != nullptr) {
+            pieces = reinterpret_cast<const int4*>(p.plan + 1);
+            n_units = p.plan->num_pieces;
+            if (p.plan->status != 0 || p.plan->heads != p.heads || p.plan->head_dim != D) {
+                if (lane == 0) raise_error(err, F3S_ERR_BAD_FORMAT);
+                n_units = 0;
+            }
+        }
+        const int total = n_units * p.groups;
         const int bi = lane % C::NBOX;  // box of this lane: 0 = a (HA chunks), 1 = b (last chunk)
         const bool vlane = lane >= C::NBOX;
         const CUtensorMap* tkv = vlane ? (bi ? &maps.vb : &maps.va) : (bi ? &maps.kb : &maps.ka);
@@ -228,20 +260,31 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         item = __shfl_sync(0xffffffffu, item, 0);
         for (;;) {
             const bool end = item >= total;
-            int w = -1, g = 0, b0 = 0, b1 = 0, nxt = total;
+            int w = -1, g = 0, b0 = 0, b1 = 0, pslot = -1, nxt = total;
             if (!end) {
                 if (lane == 0) nxt = atomicAdd(&p.hdr->counter, 1);
-                const int slot = item / p.groups;
-                g = item - slot * p.groups;
-                w = __ldg(p.order + slot);
+                const int unit = item / p.groups;
+                g = item - unit * p.groups;
+                if (pieces != nullptr) {
+                    const int4 pc = __ldg(pieces + unit);
+                    w = pc.x;
+                    b0 = pc.y;
+                    b1 = pc.z;
+                    pslot = pc.w;
+                } else {
+                    w = __ldg(p.order + unit);
+                }
                 if (w < p.q_window_base || w >= p.q_window_base + p.q_windows) {
                     if (lane == 0) raise_error(err, F3S_ERR_BAD_FORMAT);
                     aborted = true;
                     break;
                 }
-                b0 = __ldg(p.offsets + w);
-                b1 = __ldg(p.offsets + w + 1);
-                if (b0 < 0 || b1 < b0 || b1 > b_total) {
+                const int wb0 = __ldg(p.offsets + w), wb1 = __ldg(p.offsets + w + 1);
+                if (pieces == nullptr) {
+                    b0 = wb0;
+                    b1 = wb1;
+                }
+                if (wb0 < 0 || wb1 < wb0 || wb1 > b_total || b0 < wb0 || b1 < b0 || b1 > wb1) {
                     if (lane == 0) raise_error(err, F3S_ERR_BAD_FORMAT);
                     aborted = true;
                     break;
@@ -255,10 +298,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             const int z0 = g * C::HC;
             if (lane == 0) {
                 if (end) {
-                    winfo[q] = make_int4(-1, 0, 0, 0);
+                    winfo[2 * q] = make_int4(-1, 0, 0, 0);
                     mbar_arrive(qfull(q));
                 } else {
-                    winfo[q] = make_int4(w, g, b0, b1);
+                    winfo[2 * q] = make_int4(w, g, b0, b1);
+                    winfo[2 * q + 1] = make_int4(pslot, 0, 0, 0);
                     if (b1 > b0)
                         mbar_arrive_expect_tx(qfull(q), C::TILE);
                     else
@@ -342,7 +386,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     for (int k = 0;; ++k) {
         const int q = k & 1;
         if (!wait_warp(qfull(q), (k >> 1) & 1, err, p.timeout_ns)) return;
-        const int4 wi = winfo[q];
+        const int4 wi = winfo[2 * q];
+        const int pslot = winfo[2 * q + 1].x;
         if (wi.x < 0) return;
         const int w = wi.x, g = wi.y, nb = wi.w - wi.z;
         uint32_t qa[KS][4];
@@ -525,6 +570,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             if (lane == 0) mbar_arrive(mempty);
         }
 
+        if (pslot >= 0) {
+            // piece of a split window: partial (m, l, unnormalised O) of the
+            // 16 rows and this warp's head -> plan scratch, merged later
+            float* partials = reinterpret_cast<float*>(reinterpret_cast<char*>(p.plan) + p.plan->partials_off);
+            float* slot = partials + ((size_t)pslot * p.groups + g) * (size_t)(HG * 16 * (D + 2));
+            float* op = slot + (size_t)hh * 16 * D + 2 * t4;
+#pragma unroll
+            for (int jn = 0; jn < NT; ++jn) {
+                *reinterpret_cast<float2*>(op + g4 * D + jn * 8) = make_float2(o[jn][0], o[jn][1]);
+                *reinterpret_cast<float2*>(op + (g4 + 8) * D + jn * 8) = make_float2(o[jn][2], o[jn][3]);
+            }
+            if (t4 == 0) {
+                float* ml = slot + (size_t)HG * 16 * D + (size_t)hh * 32;
+                *reinterpret_cast<float2*>(ml + 2 * g4) = make_float2(m0, l0);
+                *reinterpret_cast<float2*>(ml + 2 * (g4 + 8)) = make_float2(m1, l1);
+            }
+            continue;
+        }
         // ------------------------------------------------ normalise, store --
         const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
         const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
@@ -544,6 +607,128 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 __stcs(reinterpret_cast<float2*>(dst + jn * 8), make_float2(o[jn][2] * inv1, o[jn][3] * inv1));
         }
     }
+}
+
+// ------------------------------------------------------------ plan kernels --
+
+// Per listed window: number of pieces, pieces of split windows, split flag.
+__global__ void __launch_bounds__(256) k_plan_count(const int* __restrict__ offsets, const int* __restrict__ order,
+                                                    int n, int T, int* __restrict__ npieces, int* __restrict__ nsplitp,
+                                                    int* __restrict__ nsplitw) {
+    const int i = blockIdx.x * 256 + threadIdx.x;
+    if (i >= n) return;
+    const int w = order[i];
+    const int nb = offsets[w + 1] - offsets[w];
+    const bool split = nb > T;
+    const int cnt = split ? (nb + T - 1) / T : 1;
+    npieces[i] = cnt;
+    nsplitp[i] = split ? cnt : 0;
+    nsplitw[i] = split ? 1 : 0;
+}
+
+// After the three exclusive scans (totals at index n): write the pieces and
+// the split-window records, within the plan's capacities.
+__global__ void __launch_bounds__(256) k_plan_fill(const int* __restrict__ offsets, const int* __restrict__ order,
+                                                   int n, int T, const int* __restrict__ poff,
+                                                   const int* __restrict__ soff, const int* __restrict__ woff,
+                                                   PlanHeader* ph) {
+    int4* pieces = reinterpret_cast<int4*>(ph + 1);
+    int4* splits = reinterpret_cast<int4*>(reinterpret_cast<char*>(ph) + ph->splits_off);
+    const int i = blockIdx.x * 256 + threadIdx.x;
+    if (i == 0) {
+        ph->num_pieces = poff[n];
+        ph->num_split = woff[n];
+        ph->num_split_pieces = soff[n];
+        if (poff[n] > ph->max_pieces || woff[n] > ph->max_split || soff[n] > ph->max_split_pieces)
+            ph->status = F3S_ERR_WORKSPACE;
+    }
+    if (i >= n) return;
+    if (poff[n] > ph->max_pieces || woff[n] > ph->max_split || soff[n] > ph->max_split_pieces) return;
+    const int w = order[i];
+    const int b0 = offsets[w], b1 = offsets[w + 1];
+    const int cnt = poff[i + 1] - poff[i];
+    const bool split = woff[i + 1] > woff[i];
+    for (int k = 0; k < cnt; ++k) {
+        const int lo = split ? b0 + k * T : b0;
+        const int hi = split ? min(b1, lo + T) : b1;
+        pieces[poff[i] + k] = make_int4(w, lo, hi, split ? soff[i] + k : -1);
+    }
+    if (split) splits[woff[i]] = make_int4(w, soff[i], cnt, 0);
+}
+
+// One CTA per (split window, head group): O = sum_k 2^(m_k - M) O_k /
+// sum_k 2^(m_k - M) l_k over the window's pieces, in piece order.
+template <int D>
+__global__ void __launch_bounds__(256) k_merge_pieces(const PlanHeader* __restrict__ ph, float* __restrict__ O,
+                                                      int heads, int num_nodes, int q_window_base, int q_rows) {
+    if (ph->status != 0 || ph->heads != heads || ph->head_dim != D) return;
+    const int4* splits = reinterpret_cast<const int4*>(reinterpret_cast<const char*>(ph) + ph->splits_off);
+    const float* partials = reinterpret_cast<const float*>(reinterpret_cast<const char*>(ph) + ph->partials_off);
+    const int groups = ph->groups, hg = ph->hg;
+    const size_t slot_f = (size_t)hg * 16 * (D + 2);
+    for (int unit = blockIdx.x; unit < ph->num_split * groups; unit += gridDim.x) {
+    const int sidx = unit / groups, g = unit - sidx * groups;
+    const int4 sw = splits[sidx];  // (window, first slot, pieces, -)
+    for (int e = threadIdx.x; e < hg * 16 * D; e += blockDim.x) {
+        const int hh = e / (16 * D), r = (e / D) % 16, dd = e % D;
+        const int row = 16 * sw.x + r;
+        const int64_t srow = (int64_t)row - 16 * (int64_t)q_window_base;
+        if (row >= num_nodes || srow >= q_rows) continue;
+        float M = -INFINITY;
+        for (int k = 0; k < sw.z; ++k) {
+            const float* ml = partials + ((size_t)(sw.y + k) * groups + g) * slot_f + (size_t)hg * 16 * D;
+            M = fmaxf(M, ml[hh * 32 + 2 * r]);
+        }
+        float L = 0.f, acc = 0.f;
+        for (int k = 0; k < sw.z; ++k) {
+            const float* slot = partials + ((size_t)(sw.y + k) * groups + g) * slot_f;
+            const float* ml = slot + (size_t)hg * 16 * D + hh * 32 + 2 * r;
+            const float f = fast_exp2(ml[0] - M);
+            L = fmaf(f, ml[1], L);
+            acc = fmaf(f, slot[(size_t)hh * 16 * D + r * D + dd], acc);
+        }
+        O[(srow * heads + (int64_t)g * hg + hh) * D + dd] = L > 0.f ? acc / L : 0.f;
+    }
+    }
+}
+
+__global__ void k_plan_init(PlanHeader* ph, const PlanHeader h) {
+    if (threadIdx.x == 0) *ph = h;
+}
+
+struct PlanLayout {
+    size_t pieces, splits, npieces, nsplitp, nsplitw, tiles, partials, total;
+    int max_pieces, max_split, max_split_pieces, groups, hg;
+};
+
+static int pick_head_group(int heads, int head_dim);
+
+static PlanLayout plan_layout(int num_items, int64_t num_blocks, int T, int heads, int head_dim) {
+    PlanLayout L{};
+    L.hg = pick_head_group(heads, head_dim);
+    L.groups = heads / L.hg;
+    const int64_t per_t = T > 0 ? num_blocks / T : 0;
+    L.max_pieces = (int)std::min<int64_t>(INT32_MAX / 2, (int64_t)num_items + 2 * per_t + 1);
+    L.max_split = (int)std::min<int64_t>(num_items, per_t + 1);
+    L.max_split_pieces = (int)std::min<int64_t>(INT32_MAX / 2, 2 * per_t + 1);
+    size_t off = sizeof(PlanHeader);
+    L.pieces = off;
+    off = align_up(off + (size_t)L.max_pieces * 16, 256);
+    L.splits = off;
+    off = align_up(off + (size_t)std::max(L.max_split, 1) * 16, 256);
+    const size_t nn = (size_t)num_items + 1;
+    L.npieces = off;
+    off = align_up(off + nn * 4, 256);
+    L.nsplitp = off;
+    off = align_up(off + nn * 4, 256);
+    L.nsplitw = off;
+    off = align_up(off + nn * 4, 256);
+    L.tiles = off;
+    off = align_up(off + (size_t)std::max<int64_t>(scan_tiles(num_items), 1) * 4, 256);
+    L.partials = off;
+    off = align_up(off + (size_t)L.max_split_pieces * L.groups * L.hg * 16 * (head_dim + 2) * 4, 256);
+    L.total = off;
+    return L;
 }
 
 // ------------------------------------------------------------------ host --
@@ -608,10 +793,16 @@ static int launch_variant(const void* Q, const void* K, const void* V, FwdParams
         !encode_map(&maps.va, V, prm.num_nodes, prm.heads, D, C::HA) ||
         !encode_map(&maps.vb, V, prm.num_nodes, prm.heads, D, hb))
         return F3S_ERR_INVALID_VALUE;
+    const int sms = num_sms_of_current_device();
     const int items = prm.num_items * prm.groups;
-    const int grid = std::max(1, std::min(items, num_sms_of_current_device()));
+    const int grid = prm.plan ? sms : std::max(1, std::min(items, sms));
     k_fused3s<D, HG><<<grid, kFwdThreads, C::SMEM, stream>>>(maps, prm);
     F3S_LAUNCH_CHECK();
+    if (prm.plan) {
+        k_merge_pieces<D><<<2 * sms, 256, 0, stream>>>(prm.plan, prm.O, prm.heads, prm.num_nodes, prm.q_window_base,
+                                                       prm.q_rows);
+        F3S_LAUNCH_CHECK();
+    }
     return F3S_SUCCESS;
 }
 
@@ -624,18 +815,59 @@ static int pick_head_group(int heads, int head_dim) {
     return hg;
 }
 
+int make_plan_impl(const int* offsets, const int* order, int num_items, int64_t num_blocks, int T, int heads,
+                   int head_dim, void* plan, size_t plan_bytes, cudaStream_t stream) {
+    if (num_items < 0 || num_blocks < 0 || T < 1 || heads <= 0) return F3S_ERR_INVALID_VALUE;
+    if (head_dim != 64 && head_dim != 128) return F3S_ERR_UNSUPPORTED;
+    if (!plan || (num_items > 0 && (!offsets || !order))) return F3S_ERR_INVALID_VALUE;
+    if ((reinterpret_cast<uintptr_t>(plan) & 255) != 0) return F3S_ERR_INVALID_VALUE;
+    const PlanLayout L = plan_layout(num_items, num_blocks, T, heads, head_dim);
+    if (plan_bytes < L.total) return F3S_ERR_WORKSPACE;
+    PlanHeader h{};
+    h.max_pieces = L.max_pieces;
+    h.max_split = L.max_split;
+    h.max_split_pieces = L.max_split_pieces;
+    h.max_blocks = T;
+    h.heads = heads;
+    h.head_dim = head_dim;
+    h.groups = L.groups;
+    h.hg = L.hg;
+    h.splits_off = (long long)L.splits;
+    h.partials_off = (long long)L.partials;
+    PlanHeader* ph = static_cast<PlanHeader*>(plan);
+    k_plan_init<<<1, 32, 0, stream>>>(ph, h);
+    F3S_LAUNCH_CHECK();
+    if (num_items == 0) return F3S_SUCCESS;
+    char* base = static_cast<char*>(plan);
+    int* np = reinterpret_cast<int*>(base + L.npieces);
+    int* sp = reinterpret_cast<int*>(base + L.nsplitp);
+    int* sw = reinterpret_cast<int*>(base + L.nsplitw);
+    int* tiles = reinterpret_cast<int*>(base + L.tiles);
+    const int grid = (num_items + 255) / 256;
+    k_plan_count<<<grid, 256, 0, stream>>>(offsets, order, num_items, T, np, sp, sw);
+    F3S_LAUNCH_CHECK();
+    int rc;
+    if ((rc = device_exclusive_scan(np, np, num_items, true, tiles, stream)) != F3S_SUCCESS) return rc;
+    if ((rc = device_exclusive_scan(sp, sp, num_items, true, tiles, stream)) != F3S_SUCCESS) return rc;
+    if ((rc = device_exclusive_scan(sw, sw, num_items, true, tiles, stream)) != F3S_SUCCESS) return rc;
+    k_plan_fill<<<grid, 256, 0, stream>>>(offsets, order, num_items, T, np, sp, sw, ph);
+    F3S_LAUNCH_CHECK();
+    return F3S_SUCCESS;
+}
+
 int forward_impl(const void* Q, const void* K, const void* V, float* O, const int* offsets, const int* cols,
-                 const int* order, const uint8_t* col_hints, int num_items, int num_nodes, int heads, int head_dim,
-                 int q_window_base, int q_rows, void* ws, size_t ws_bytes, cudaStream_t stream,
-                 uint64_t timeout_ns) {
+                 const int* order, const uint8_t* col_hints, const void* plan, int num_items, int num_nodes,
+                 int heads, int head_dim, int q_window_base, int q_rows, void* ws, size_t ws_bytes,
+                 cudaStream_t stream, uint64_t timeout_ns) {
     if (num_items < 0 || num_nodes < 0 || heads <= 0 || q_window_base < 0 || q_rows < 0)
         return F3S_ERR_INVALID_VALUE;
     if (head_dim != 64 && head_dim != 128) return F3S_ERR_UNSUPPORTED;
     if (!ws) return F3S_ERR_INVALID_VALUE;
     if (ws_bytes < kWsHeaderBytes) return F3S_ERR_WORKSPACE;
     if ((int64_t)heads * head_dim * 2 * 16 > (int64_t)1 << 40) return F3S_ERR_TOO_LARGE;
-    if (num_items == 0 || num_nodes == 0 || q_rows == 0) return F3S_SUCCESS;
-    if (!Q || !K || !V || !O || !offsets || !cols || !order) return F3S_ERR_INVALID_VALUE;
+    if (plan) num_items = 0;  // the plan lists the work
+    if ((!plan && num_items == 0) || num_nodes == 0 || q_rows == 0) return F3S_SUCCESS;
+    if (!Q || !K || !V || !O || !offsets || !cols || (!plan && !order)) return F3S_ERR_INVALID_VALUE;
     auto misaligned = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) != 0; };
     if (misaligned(Q) || misaligned(K) || misaligned(V) || misaligned(O)) return F3S_ERR_INVALID_VALUE;
     const int hg = pick_head_group(heads, head_dim);
@@ -644,6 +876,7 @@ int forward_impl(const void* Q, const void* K, const void* V, float* O, const in
     prm.offsets = offsets;
     prm.cols = cols;
     prm.order = order;
+    prm.plan = static_cast<PlanHeader*>(const_cast<void*>(plan));
     prm.hints = col_hints;
     prm.hdr = static_cast<WsHeader*>(ws);
     prm.timeout_ns = timeout_ns;
@@ -707,13 +940,27 @@ extern "C" {
 
 size_t f3s_forward_workspace_size(void) { return f3s::kWsHeaderBytes; }
 
+size_t f3s_plan_size(int32_t num_items, int64_t num_blocks, int32_t max_blocks_per_piece, int32_t heads,
+                     int32_t head_dim) {
+    if (num_items < 0 || num_blocks < 0 || max_blocks_per_piece < 1 || heads <= 0) return 0;
+    if (head_dim != 64 && head_dim != 128) return 0;
+    return f3s::plan_layout(num_items, num_blocks, max_blocks_per_piece, heads, head_dim).total;
+}
+
+int f3s_make_plan(const int32_t* d_window_offsets, const int32_t* d_order, int32_t num_items, int64_t num_blocks,
+                  int32_t max_blocks_per_piece, int32_t heads, int32_t head_dim, void* d_plan, size_t plan_bytes,
+                  f3s_stream_t stream) {
+    return f3s::make_plan_impl(d_window_offsets, d_order, num_items, num_blocks, max_blocks_per_piece, heads,
+                               head_dim, d_plan, plan_bytes, (cudaStream_t)stream);
+}
+
 int f3s_forward(const void* d_Q, const void* d_K, const void* d_V, float* d_O, const int32_t* d_window_offsets,
-                const int32_t* d_block_cols, const int32_t* d_order, const uint8_t* d_col_hints, int32_t num_items,
-                int32_t num_nodes, int32_t heads, int32_t head_dim, int32_t q_window_base, int32_t q_rows,
-                void* d_workspace, size_t workspace_bytes, f3s_stream_t stream) {
-    return f3s::forward_impl(d_Q, d_K, d_V, d_O, d_window_offsets, d_block_cols, d_order, d_col_hints, num_items,
-                             num_nodes, heads, head_dim, q_window_base, q_rows, d_workspace, workspace_bytes,
-                             (cudaStream_t)stream, f3s::kWaitTimeoutNs);
+                const int32_t* d_block_cols, const int32_t* d_order, const uint8_t* d_col_hints, const void* d_plan,
+                int32_t num_items, int32_t num_nodes, int32_t heads, int32_t head_dim, int32_t q_window_base,
+                int32_t q_rows, void* d_workspace, size_t workspace_bytes, f3s_stream_t stream) {
+    return f3s::forward_impl(d_Q, d_K, d_V, d_O, d_window_offsets, d_block_cols, d_order, d_col_hints, d_plan,
+                             num_items, num_nodes, heads, head_dim, q_window_base, q_rows, d_workspace,
+                             workspace_bytes, (cudaStream_t)stream, f3s::kWaitTimeoutNs);
 }
 
 int f3s_selftest_wait_timeout(uint64_t timeout_ns, void* d_workspace, size_t workspace_bytes, f3s_stream_t stream) {

@@ -153,6 +153,9 @@ int f3s_window_order(const int32_t* d_window_offsets, int32_t num_row_windows, i
  *            each must lie in [q_window_base, q_window_base + ceil(q_rows/16)))
  *   d_col_hints optional uint8[nrw] per block column L2 eviction hint from
  *            f3s_column_hints (NULL: no hint); affects speed only.
+ *   d_plan   optional plan from f3s_make_plan (NULL: one work item per entry
+ *            of d_order).  With a plan, d_order / num_items are not used: the
+ *            plan lists the windows, heavy ones cut into pieces.
  *   q_window_base / q_rows: 0 / num_nodes on one GPU; a rank's slab when the
  *            windows are sharded across GPUs.
  * head_dim in {64, 128}; heads >= 1.  No padding of any tensor is needed:
@@ -162,9 +165,29 @@ int f3s_window_order(const int32_t* d_window_offsets, int32_t num_row_windows, i
 size_t f3s_forward_workspace_size(void);
 int f3s_forward(const void* d_Q, const void* d_K, const void* d_V, float* d_O,
                 const int32_t* d_window_offsets, const int32_t* d_block_cols, const int32_t* d_order,
-                const uint8_t* d_col_hints, int32_t num_items, int32_t num_nodes, int32_t heads,
-                int32_t head_dim, int32_t q_window_base, int32_t q_rows, void* d_workspace,
+                const uint8_t* d_col_hints, const void* d_plan, int32_t num_items, int32_t num_nodes,
+                int32_t heads, int32_t head_dim, int32_t q_window_base, int32_t q_rows, void* d_workspace,
                 size_t workspace_bytes, f3s_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Work plan for f3s_forward (no reference counterpart: the reference gives
+ * each window one CTA, so one heavy window bounds the kernel's run time).
+ *
+ * For the windows in d_order[0 .. num_items) (kept in that order), a window
+ * with more than max_blocks_per_piece active blocks becomes
+ * ceil(blocks / max_blocks_per_piece) pieces of consecutive blocks, each its
+ * own work item; the pieces' partial softmax states are merged (in piece
+ * order: the result is deterministic) after the fused kernel.  num_blocks is
+ * an upper bound on the active blocks of the listed windows (sizes the
+ * plan).  The plan is built on the device; compute it once per graph and
+ * window set, for one (heads, head_dim).  d_plan must be 256-byte aligned;
+ * a plan is used by one forward at a time.
+ * ---------------------------------------------------------------------- */
+size_t f3s_plan_size(int32_t num_items, int64_t num_blocks, int32_t max_blocks_per_piece, int32_t heads,
+                     int32_t head_dim);
+int f3s_make_plan(const int32_t* d_window_offsets, const int32_t* d_order, int32_t num_items,
+                  int64_t num_blocks, int32_t max_blocks_per_piece, int32_t heads, int32_t head_dim,
+                  void* d_plan, size_t plan_bytes, f3s_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Per block column L2 eviction hints for f3s_forward (no reference

@@ -195,7 +195,8 @@ inline void float2half(const float* in, void* out, int64_t n, cudaStream_t strea
 inline void forward(const void* Q, const void* K, const void* V, float* O, const int* window_offsets,
                     const int* block_cols, const int* order, int num_items, int num_nodes, int heads, int head_dim,
                     void* workspace, size_t workspace_bytes, cudaStream_t stream = 0) {
-    check(f3s_forward(Q, K, V, O, window_offsets, block_cols, order, nullptr, num_items, num_nodes, heads, head_dim, 0,
+    check(f3s_forward(Q, K, V, O, window_offsets, block_cols, order, nullptr, nullptr, num_items, num_nodes, heads,
+                      head_dim, 0,
                       num_nodes, workspace, workspace_bytes, reinterpret_cast<f3s_stream_t>(stream)),
           "f3s_forward");
 }

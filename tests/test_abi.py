@@ -46,9 +46,9 @@ def test_host_only_queries(lib):
 
 def test_invalid_arguments_are_rejected_without_touching_the_gpu(lib):
     # validated on the host before any CUDA call
-    assert lib.f3s_forward(None, None, None, None, None, None, None, None, 1, 10, 1, 96, 0, 10, None, 0,
+    assert lib.f3s_forward(None, None, None, None, None, None, None, None, None, 1, 10, 1, 96, 0, 10, None, 0,
                            None) == _lib.F3S_ERR_UNSUPPORTED
-    assert lib.f3s_forward(None, None, None, None, None, None, None, None, 1, 10, 1, 64, 0, 10, None, 0,
+    assert lib.f3s_forward(None, None, None, None, None, None, None, None, None, 1, 10, 1, 64, 0, 10, None, 0,
                            None) == _lib.F3S_ERR_INVALID_VALUE
     assert lib.f3s_convert(None, None, -1, 0, None, None, None, 0, None, None) == _lib.F3S_ERR_INVALID_VALUE
     assert lib.f3s_window_order(None, -3, None, None, 0, None) == _lib.F3S_ERR_INVALID_VALUE

@@ -1,0 +1,98 @@
+"""Work plans: heavy windows cut into pieces whose partial softmax states are
+merged after the fused kernel.  Same parity bar as every forward test
+(max-abs 2e-2, rel-L2 1e-3 against the reference's CPU ground truth), and
+deterministic: the merge runs in piece order."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import fused3s_b200 as F
+from conftest import MAX_ABS_TOL, REL_L2_TOL
+from fused3s_b200 import _lib
+from fused3s_b200 import graphs as G
+
+pytestmark = pytest.mark.gpu
+
+
+def feats(n, h, d, kind="uniform", seed=42):
+    q, k, v = G.make_features(n, h, d, kind=kind, seed=seed, device="cpu")
+    return q.numpy(), k.numpy(), v.numpy()
+
+
+def gpu(*a):
+    return [torch.from_numpy(np.ascontiguousarray(x)).cuda() for x in a]
+
+
+def parity(o, ref, what):
+    ma, rl = oracle.max_abs(o, ref), oracle.rel_l2(o, ref)
+    assert ma <= MAX_ABS_TOL and rl <= REL_L2_TOL, f"{what}: maxabs={ma:.3e} relL2={rl:.3e}"
+
+
+@pytest.mark.parametrize("heads,head_dim,T", [(1, 64, 3), (2, 64, 5), (8, 64, 4), (4, 128, 7), (3, 64, 16)])
+def test_plan_matches_oracle(lib, heads, head_dim, T):
+    g = G.powerlaw_graph(num_nodes=2003, directed_edges=20000, max_degree=500, seed=heads + T)
+    q, k, v = feats(g.num_nodes, heads, head_dim)
+    fmt = F.convert_csr_to_block_sparse(g.num_nodes, g.row_ptr, g.col_ind)
+    plan = F.make_plan(fmt, heads, head_dim, max_blocks=T)
+    Q, K, V = gpu(q, k, v)
+    o = F.fused3s_forward(Q, K, V, fmt, plan=plan, check_status=True).cpu().numpy()
+    off, cols = fmt.to_host()
+    assert np.diff(off).max() > T  # something was split
+    ref = oracle.block_attention(g.num_nodes, q.astype(np.float32), k.astype(np.float32), v.astype(np.float32),
+                                 off, cols, threads=8)
+    parity(o, ref, f"H={heads} d={head_dim} T={T}")
+    o2 = F.fused3s_forward(Q, K, V, fmt, plan=plan, check_status=True).cpu().numpy()
+    assert np.array_equal(o, o2)  # deterministic
+
+
+def test_plan_without_splits_is_bit_identical(lib):
+    g = G.make_graph("c1")
+    q, k, v = feats(g.num_nodes, 1, 64)
+    fmt = F.convert_csr_to_block_sparse(g.num_nodes, g.row_ptr, g.col_ind)
+    Q, K, V = gpu(q, k, v)
+    plan = F.make_plan(fmt, 1, 64, max_blocks=1 << 20)
+    a = F.fused3s_forward(Q, K, V, fmt, check_status=True).cpu()
+    b = F.fused3s_forward(Q, K, V, fmt, plan=plan, check_status=True).cpu()
+    assert torch.equal(a, b)
+
+
+def test_plan_slabs_equal_full_planned(lib):
+    """Per-rank plans over contiguous window slabs reproduce the full planned
+    output bit for bit (the piece cut depends only on the window)."""
+    g = G.powerlaw_graph(num_nodes=4099, directed_edges=40000, max_degree=800, seed=9)
+    q, k, v = feats(g.num_nodes, 2, 64)
+    fmt = F.convert_csr_to_block_sparse(g.num_nodes, g.row_ptr, g.col_ind)
+    Q, K, V = gpu(q, k, v)
+    T = 6
+    full = F.fused3s_forward(Q, K, V, fmt, plan=F.make_plan(fmt, 2, 64, max_blocks=T), check_status=True).cpu()
+    order = F.generate_balanced_window_order(fmt)
+    parts = []
+    cuts = [0, 50, 120, fmt.num_row_windows]
+    for lo, hi in zip(cuts[:-1], cuts[1:]):
+        r0, r1 = 16 * lo, min(16 * hi, g.num_nodes)
+        mine = order[(order >= lo) & (order < hi)].contiguous()
+        plan = F.make_plan(fmt, 2, 64, order=mine, max_blocks=T)
+        parts.append(F.fused3s_forward(Q[r0:r1].contiguous(), K, V, fmt, q_window_base=lo, plan=plan,
+                                       check_status=True).cpu())
+    assert torch.equal(torch.cat(parts), full)
+
+
+def test_plan_overflow_is_reported(lib):
+    """A plan sized with a too-small block bound records an error instead of
+    writing past its end, and the forward refuses it."""
+    g = G.make_graph("c1")
+    fmt = F.convert_csr_to_block_sparse(g.num_nodes, g.row_ptr, g.col_ind)
+    order = F.generate_balanced_window_order(fmt)
+    n = fmt.num_row_windows
+    size = lib.f3s_plan_size(n, 1, 1, 1, 64)  # claims one block in total
+    buf = torch.zeros(size, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.f3s_make_plan(fmt.window_offsets.data_ptr(), order.data_ptr(), n, 1, 1, 1, 64, buf.data_ptr(), size,
+                             stream) == 0
+    plan = F.ForwardPlan(buf, 1, 64, 1)
+    q, k, v = (t.cuda() for t in G.make_features(g.num_nodes, 1, 64))
+    with pytest.raises(_lib.Fused3SError) as e:
+        F.fused3s_forward(q, k, v, fmt, plan=plan, check_status=True)
+    assert e.value.status == _lib.F3S_ERR_BAD_FORMAT
+    F.fused3s_forward(q, k, v, fmt, check_status=True)  # device still fine
