@@ -45,6 +45,27 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
+_RESULT_OUT = None
+
+
+def emit(record: dict) -> None:
+    """Write the one JSON result line to the process's real stdout."""
+    out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
+    out.write(json.dumps(record) + "\n")
+    out.flush()
+
+
+def route_stdout_to_stderr() -> None:
+    """Keep the real stdout for the result line only: file descriptor 1 is
+    pointed at stderr so banners printed by libraries (NCCL's version line,
+    for one) cannot mix with it."""
+    global _RESULT_OUT
+    sys.stdout.flush()
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    sys.stdout = sys.stderr
+
+
 def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
@@ -246,7 +267,7 @@ def run_reference(args):
                                    f"to all {B} blocks x {cfg.heads} heads"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -467,7 +488,7 @@ def run_ours(args):
         }
         if gather_ms is not None:
             result["allgather_o_ms"] = gather_ms
-        print(json.dumps(result), flush=True)
+        emit(result)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -491,6 +512,7 @@ def main(argv=None):
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU work for cpu_baseline")
     ap.add_argument("--ref-step-budget", type=float, default=3.0, help="seconds of CPU work per reference step")
     args = ap.parse_args(argv)
+    route_stdout_to_stderr()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
