@@ -319,13 +319,13 @@ def run_ours(args):
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
     n_items = int(my_order.numel())
-    # L2 eviction hints per block column: computed once per graph and rank
+    # L2 eviction hints per block: computed once per graph and rank
     hints = None
     hints_ms = None
     if args.l2_hints == "on":
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        hints = F.column_hints(fmt, H, d, order=my_order)
+        hints = F.block_hints(fmt, H, d, order=my_order)
         torch.cuda.synchronize()
         hints_ms = (time.perf_counter() - t0) * 1e3
     hints_ptr = hints.data_ptr() if hints is not None else None
@@ -343,9 +343,12 @@ def run_ours(args):
     plan_ptr = plan.buffer.data_ptr() if plan is not None else None
 
     def step():
+        # launches on the current stream (the capture stream while a graph
+        # is being recorded)
         st = lib.f3s_forward(Q.data_ptr(), Kf.data_ptr(), Vf.data_ptr(), O.data_ptr(),
                              fmt.window_offsets.data_ptr(), fmt.cols_ptr, my_order.data_ptr(), hints_ptr,
-                             plan_ptr, n_items, N, H, d, lo, r1 - r0, ws.data_ptr(), ws.numel(), sptr)
+                             plan_ptr, n_items, N, H, d, lo, r1 - r0, ws.data_ptr(), ws.numel(),
+                             torch.cuda.current_stream(dev).cuda_stream)
         if st != 0:
             raise _lib.Fused3SError(st, "f3s_forward")
 
@@ -354,6 +357,21 @@ def run_ours(args):
     st = lib.f3s_workspace_status(ws.data_ptr(), sptr)
     if st != 0:
         raise _lib.Fused3SError(st, "f3s_forward (device, warm-up)")
+    # The step as a CUDA graph (workspace reset + fused kernel + merge), so
+    # small graphs are not bound by host launch latency.
+    run = step
+    graph = None
+    if args.graph == "on":
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            step()
+        stream.wait_stream(side)
+        with torch.cuda.graph(graph):
+            step()
+        torch.cuda.synchronize()
+        run = graph.replay
 
     uuid = None
     try:
@@ -367,7 +385,7 @@ def run_ours(args):
     with ClockSampler(uuid) as clk:
         evs[0].record(stream)
         for i in range(args.steps):
-            step()
+            run()
             evs[i + 1].record(stream)
         torch.cuda.synchronize()
     if world > 1:
@@ -400,7 +418,7 @@ def run_ours(args):
             dQ.copy_(hQ, non_blocking=True)
             dK.copy_(hK, non_blocking=True)
             dV.copy_(hV, non_blocking=True)
-            F.fused3s_forward(dQ, dK, dV, fmt, order=my_order, out=O, q_window_base=lo, col_hints=hints,
+            F.fused3s_forward(dQ, dK, dV, fmt, order=my_order, out=O, q_window_base=lo, block_hints=hints,
                               plan=plan)
             hO.copy_(O, non_blocking=True)
 
@@ -473,7 +491,7 @@ def run_ours(args):
                        "parallelism": f"row-window shards x{world}, K/V replicated",
                        "l2": "inputs larger than L2" if (Kf.numel() + Vf.numel()) * 2 > 126e6 else
                              "inputs fit in L2 (no flush)",
-                       "convert_ms": convert_ms, "order_ms": order_ms, "l2_hints": args.l2_hints,
+                       "convert_ms": convert_ms, "order_ms": order_ms, "l2_hints": args.l2_hints, "cuda_graph": args.graph,
                        "hints_ms": hints_ms, "split": args.split,
                        "piece_blocks": plan.max_blocks if plan is not None else None, "plan_ms": plan_ms},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
@@ -483,7 +501,7 @@ def run_ours(args):
                          "tensor_frac": flops_launch / (kern_ms / 1e3) / 1e12 / tc_peak},
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * (2 if plan is not None else 1),
             "clocks": clocks,
         }
         if gather_ms is not None:
@@ -503,10 +521,12 @@ def main(argv=None):
     ap.add_argument("--config", default="c4", choices=["c1", "c2", "c3", "c4", "c5", "c4s"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gather", action="store_true", help="also time the NCCL all-gather of O (N > 1)")
+    ap.add_argument("--graph", default="on", choices=["on", "off"],
+                    help="replay the timed step as a CUDA graph")
     ap.add_argument("--split", default="auto",
                     help="cut windows above this many blocks into pieces: auto, off or a number")
     ap.add_argument("--l2-hints", default="on", choices=["on", "off"],
-                    help="per block column L2 eviction hints (computed once per graph)")
+                    help="per block L2 eviction hints (computed once per graph)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU work for cpu_baseline")

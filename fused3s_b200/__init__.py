@@ -11,7 +11,7 @@ from .api import (
     ForwardPlan,
     Fused3SError,
     auto_piece_blocks,
-    column_hints,
+    block_hints,
     convert_csr_to_block_sparse,
     f3s_1tb1rw_kernel,
     float2half,
@@ -29,7 +29,7 @@ __all__ = [
     "ForwardPlan",
     "Fused3SError",
     "auto_piece_blocks",
-    "column_hints",
+    "block_hints",
     "convert_csr_to_block_sparse",
     "f3s_1tb1rw_kernel",
     "make_plan",

@@ -44,8 +44,8 @@ SIGNATURES = {
                                    _SZ, _P]),
     "f3s_plan_size": (_SZ, [_I32, _I64, _I32, _I32, _I32]),
     "f3s_make_plan": (ctypes.c_int, [_P, _P, _I32, _I64, _I32, _I32, _I32, _P, _SZ, _P]),
-    "f3s_column_hints_workspace_size": (_SZ, [_I32]),
-    "f3s_column_hints": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I64, _I64, _P, _P, _SZ, _P]),
+    "f3s_block_hints_workspace_size": (_SZ, [_I32]),
+    "f3s_block_hints": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I64, _I64, _P, _P, _SZ, _P]),
     "f3s_1tb1rw_launch": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _P]),
     "f3s_half_from_float": (ctypes.c_int, [_P, _P, _I64, _P]),
     "f3s_selftest_wait_timeout": (ctypes.c_int, [_U64, _P, _SZ, _P]),

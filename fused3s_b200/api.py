@@ -197,27 +197,29 @@ def _as_nhd(t: torch.Tensor) -> torch.Tensor:
     return t.unsqueeze(1) if t.dim() == 2 else t
 
 
-def column_hints(fmt: BlockSparseFormat, heads: int, head_dim: int, order: Optional[torch.Tensor] = None,
-                 l2_fraction: float = 0.5) -> torch.Tensor:
-    """Per block column L2 eviction hints (uint8[nrw]) for the windows in
-    `order` (default: all): the most popular columns that fit in
-    `l2_fraction` of the device's L2 are kept, single-use columns streamed.
-    Computed once per graph; pass to fused3s_forward(col_hints=...)."""
+def block_hints(fmt: BlockSparseFormat, heads: int, head_dim: int, order: Optional[torch.Tensor] = None,
+                l2_fraction: float = 0.5) -> torch.Tensor:
+    """L2 eviction hints, one per active block (uint8[num_blocks]), for the
+    windows in `order` (default: all).  A block's hint is its column's: the
+    most popular block columns that fit in `l2_fraction` of the device's L2
+    are kept, columns used by a single listed window streamed.  Computed once
+    per graph; pass to fused3s_forward(block_hints=...)."""
     lib = _lib.load()
     device = fmt.window_offsets.device
     nrw = fmt.num_row_windows
     if order is None:
         order = torch.arange(nrw, dtype=torch.int32, device=device)
     order = order.to(device=device, dtype=torch.int32).contiguous()
-    hints = torch.zeros(max(nrw, 1), dtype=torch.uint8, device=device)
+    nb = int(fmt.num_blocks)
+    hints = torch.zeros(max(nb, 1), dtype=torch.uint8, device=device)
     l2 = torch.cuda.get_device_properties(device).L2_cache_size
-    ws = _WS.get(device, "hints", lib.f3s_column_hints_workspace_size(nrw))
+    ws = _WS.get(device, "hints", lib.f3s_block_hints_workspace_size(nrw))
     with torch.cuda.device(device):
-        st = lib.f3s_column_hints(_ptr(fmt.window_offsets), fmt.cols_ptr, _ptr(order), int(order.numel()), nrw,
-                                  16 * heads * head_dim * 2 * 2, int(l2 * l2_fraction), _ptr(hints), _ptr(ws),
-                                  ws.numel(), _stream_ptr(device))
-    check(st, "f3s_column_hints")
-    return hints[:nrw]
+        st = lib.f3s_block_hints(_ptr(fmt.window_offsets), fmt.cols_ptr, _ptr(order), int(order.numel()), nrw,
+                                 16 * heads * head_dim * 2 * 2, int(l2 * l2_fraction), _ptr(hints), _ptr(ws),
+                                 ws.numel(), _stream_ptr(device))
+    check(st, "f3s_block_hints")
+    return hints[:nb]
 
 
 @dataclasses.dataclass
@@ -231,12 +233,13 @@ class ForwardPlan:
 
 
 def auto_piece_blocks(num_blocks: int, device=None) -> int:
-    """Piece size: a quarter of one SM's share of the blocks (so no single
-    window can hold one SM much past the others), never below 1024 blocks
-    (so the partial write stays a small overhead)."""
+    """Piece size: a quarter of one SM's share of the blocks, so no single
+    window can hold one SM much past the others; never below 16 blocks (a
+    piece's partial state is about one block's K/V bytes, so a piece of 16
+    blocks moves at most ~6 % more)."""
     device = _default_device(device)
     sms = torch.cuda.get_device_properties(device).multi_processor_count
-    return max(1024, -(-int(num_blocks) // (4 * sms)))
+    return max(16, -(-int(num_blocks) // (4 * sms)))
 
 
 def make_plan(fmt: BlockSparseFormat, heads: int, head_dim: int, order: Optional[torch.Tensor] = None,
@@ -266,7 +269,7 @@ def make_plan(fmt: BlockSparseFormat, heads: int, head_dim: int, order: Optional
 def fused3s_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: BlockSparseFormat,
                     order: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
                     q_window_base: int = 0, check_status: bool = False,
-                    col_hints: Optional[torch.Tensor] = None, plan: Optional[ForwardPlan] = None) -> torch.Tensor:
+                    block_hints: Optional[torch.Tensor] = None, plan: Optional[ForwardPlan] = None) -> torch.Tensor:
     """O = block-sparse softmax(Q K^T) V, fused (the fused3s_v2 path).
 
     Q: fp16 [q_rows, H, d] (or [q_rows, d] for one head) holding rows
@@ -275,13 +278,13 @@ def fused3s_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: Bloc
        the balanced order).  Returns fp32 O shaped like Q; rows of the listed
        windows are written in full (zeros for windows with no block).
     check_status: synchronise and raise if a kernel recorded an error.
-    col_hints: optional uint8[nrw] from column_hints() (speed only).
+    block_hints: optional uint8[num_blocks] from block_hints() (speed only).
     plan: optional ForwardPlan from make_plan(); it then lists the windows
        (order is ignored) and heavy windows run as several pieces."""
     if plan is not None and (plan.heads, plan.head_dim) != (_as_nhd(Q).shape[1], _as_nhd(Q).shape[2]):
         raise ValueError("plan was made for other heads / head_dim")
-    if col_hints is not None and (col_hints.dtype != torch.uint8 or col_hints.numel() < fmt.num_row_windows):
-        raise ValueError("col_hints must be uint8 with one entry per row window")
+    if block_hints is not None and (block_hints.dtype != torch.uint8 or block_hints.numel() < fmt.num_blocks):
+        raise ValueError("block_hints must be uint8 with one entry per active block")
     lib = _lib.load()
     _check_features(Q, K, V)
     q3, k3 = _as_nhd(Q), _as_nhd(K)
@@ -308,7 +311,7 @@ def fused3s_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: Bloc
     ws = _WS.get(device, "forward", lib.f3s_forward_workspace_size())
     with torch.cuda.device(device):
         st = lib.f3s_forward(_ptr(Q), _ptr(K), _ptr(V), _ptr(out), _ptr(fmt.window_offsets),
-                             fmt.cols_ptr, _ptr(order), _ptr(col_hints), None if plan is None else _ptr(plan.buffer),
+                             fmt.cols_ptr, _ptr(order), _ptr(block_hints), None if plan is None else _ptr(plan.buffer),
                              int(order.numel()), num_nodes, heads,
                              head_dim, q_window_base, q_rows, _ptr(ws), ws.numel(), _stream_ptr(device))
         check(st, "f3s_forward")

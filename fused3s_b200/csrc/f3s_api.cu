@@ -22,7 +22,7 @@ int num_sms_of_current_device() {
 }
 
 int forward_impl(const void* Q, const void* K, const void* V, float* O, const int* offsets, const int* cols,
-                 const int* order, const uint8_t* col_hints, const void* plan, int num_items, int num_nodes,
+                 const int* order, const uint8_t* block_hints, const void* plan, int num_items, int num_nodes,
                  int heads, int head_dim, int q_window_base, int q_rows, void* ws, size_t ws_bytes,
                  cudaStream_t stream, uint64_t timeout_ns);
 

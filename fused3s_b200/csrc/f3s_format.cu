@@ -516,18 +516,20 @@ static int window_order_impl(const int32_t* d_offsets, int32_t nrw, int32_t* d_o
 }
 
 // =========================================================================
-// L2 eviction hints per block column.
+// L2 eviction hints per block.
 //
 // A block column's K/V tile is read once per window that lists it.  Columns
 // listed by many windows are worth keeping in L2; columns listed by a single
 // window are never reused.  popularity[c] = number of listed windows that
 // reference c; the most popular columns, up to an L2 byte budget, get hint 1
 // (evict-last), single-use columns hint 2 (evict-first), the rest hint 0.
+// The hint is stored per block (hint of the block's column), so the fused
+// kernel loads it alongside the block's column index instead of after it.
 //   k_hint_popularity  one warp per listed window, atomics per block
 //   k_hint_histogram   histogram of min(popularity, 4095)
-//   k_hint_threshold   one thread: the smallest popularity whose columns
-//                      still fit the budget
-//   k_hint_mark        writes the hints
+//   k_hint_threshold   one CTA: the smallest popularity whose columns (with
+//                      all more popular ones) still fit the budget
+//   k_hint_mark        writes the per-block hints
 // =========================================================================
 
 constexpr int kHintBins = 4096;
@@ -555,24 +557,45 @@ __global__ void __launch_bounds__(256) k_hint_histogram(const int* __restrict__ 
         if (h[i]) atomicAdd(&hist[i], h[i]);
 }
 
-__global__ void k_hint_threshold(const int* __restrict__ hist, int64_t budget_cols, int* __restrict__ thr) {
-    if (threadIdx.x != 0) return;
-    int64_t cum = 0;
-    int t = kHintBins;  // nothing hot
-    for (int b = kHintBins - 1; b >= 2; --b) {
-        if (cum + hist[b] > budget_cols) break;
-        cum += hist[b];
-        t = b;
+// T = the smallest bin b >= 2 with sum(hist[b..]) <= budget (kHintBins if
+// none): those columns, the most popular, fit the budget together.
+__global__ void __launch_bounds__(1024) k_hint_threshold(const int* __restrict__ hist, int64_t budget_cols,
+                                                         int* __restrict__ thr) {
+    __shared__ int scratch[1024 / 32 + 1];
+    __shared__ int best;
+    constexpr int kPer = kHintBins / 1024;
+    // thread t owns bins [kHintBins - kPer (t + 1), kHintBins - kPer t), walked downwards
+    const int top = kHintBins - kPer * threadIdx.x;
+    int v[kPer];
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        v[i] = hist[top - 1 - i];
+        sum += v[i];
     }
-    *thr = t;
+    if (threadIdx.x == 0) best = kHintBins;
+    int total;
+    int above = block_exclusive_scan<1024>(sum, total, scratch);  // columns in higher bins
+    int local = kHintBins;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        above += v[i];
+        const int b = top - 1 - i;
+        if (b >= 2 && (int64_t)above <= budget_cols) local = b;
+    }
+    atomicMin(&best, local);
+    __syncthreads();
+    if (threadIdx.x == 0) *thr = best;
 }
 
-__global__ void __launch_bounds__(256) k_hint_mark(const int* __restrict__ pop, int nrw,
+__global__ void __launch_bounds__(256) k_hint_mark(const int* __restrict__ pop, const int* __restrict__ cols,
+                                                   const int* __restrict__ offsets, int nrw,
                                                    const int* __restrict__ thr, uint8_t* __restrict__ hints) {
     const int t = *thr;
-    for (int c = blockIdx.x * 256 + threadIdx.x; c < nrw; c += gridDim.x * 256) {
-        const int p = pop[c];
-        hints[c] = (uint8_t)(p >= t ? 1 : (p == 1 ? 2 : 0));
+    const int nb = offsets[nrw];
+    for (int b = blockIdx.x * 256 + threadIdx.x; b < nb; b += gridDim.x * 256) {
+        const int q = pop[cols[b]];
+        hints[b] = (uint8_t)(q >= t ? 1 : (q == 1 ? 2 : 0));
     }
 }
 
@@ -592,9 +615,9 @@ static HintLayout hint_layout(int32_t nrw) {
     return L;
 }
 
-static int column_hints_impl(const int32_t* d_offsets, const int32_t* d_cols, const int32_t* d_order,
-                             int32_t num_items, int32_t nrw, int64_t bytes_per_column, int64_t l2_budget_bytes,
-                             uint8_t* d_hints, void* d_workspace, size_t workspace_bytes, cudaStream_t stream) {
+static int block_hints_impl(const int32_t* d_offsets, const int32_t* d_cols, const int32_t* d_order,
+                            int32_t num_items, int32_t nrw, int64_t bytes_per_column, int64_t l2_budget_bytes,
+                            uint8_t* d_hints, void* d_workspace, size_t workspace_bytes, cudaStream_t stream) {
     if (nrw < 0 || num_items < 0 || bytes_per_column <= 0 || l2_budget_bytes < 0) return F3S_ERR_INVALID_VALUE;
     if (nrw == 0) return F3S_SUCCESS;
     if (!d_offsets || !d_cols || !d_hints || !d_workspace || (num_items > 0 && !d_order))
@@ -611,12 +634,12 @@ static int column_hints_impl(const int32_t* d_offsets, const int32_t* d_cols, co
         k_hint_popularity<<<(num_items + 7) / 8, 256, 0, stream>>>(d_offsets, d_cols, d_order, num_items, pop);
         F3S_LAUNCH_CHECK();
     }
-    const int grid = std::max(1, std::min((nrw + 255) / 256, num_sms_of_current_device() * 4));
-    k_hint_histogram<<<grid, 256, 0, stream>>>(pop, nrw, hist);
+    const int sms = num_sms_of_current_device();
+    k_hint_histogram<<<std::max(1, std::min((nrw + 255) / 256, sms * 4)), 256, 0, stream>>>(pop, nrw, hist);
     F3S_LAUNCH_CHECK();
-    k_hint_threshold<<<1, 32, 0, stream>>>(hist, l2_budget_bytes / bytes_per_column, thr);
+    k_hint_threshold<<<1, 1024, 0, stream>>>(hist, l2_budget_bytes / bytes_per_column, thr);
     F3S_LAUNCH_CHECK();
-    k_hint_mark<<<grid, 256, 0, stream>>>(pop, nrw, thr, d_hints);
+    k_hint_mark<<<sms * 8, 256, 0, stream>>>(pop, d_cols, d_offsets, nrw, thr, d_hints);
     F3S_LAUNCH_CHECK();
     return F3S_SUCCESS;
 }
@@ -701,17 +724,17 @@ int f3s_convert(const int32_t* d_row_ptr, const int32_t* d_col_ind, int32_t num_
                              d_workspace, workspace_bytes, h_num_blocks, (cudaStream_t)stream);
 }
 
-size_t f3s_column_hints_workspace_size(int32_t num_row_windows) {
+size_t f3s_block_hints_workspace_size(int32_t num_row_windows) {
     if (num_row_windows < 0) return 0;
     return f3s::hint_layout(num_row_windows).total;
 }
 
-int f3s_column_hints(const int32_t* d_window_offsets, const int32_t* d_block_cols, const int32_t* d_order,
-                     int32_t num_items, int32_t num_row_windows, int64_t bytes_per_column, int64_t l2_budget_bytes,
-                     uint8_t* d_col_hints, void* d_workspace, size_t workspace_bytes, f3s_stream_t stream) {
-    return f3s::column_hints_impl(d_window_offsets, d_block_cols, d_order, num_items, num_row_windows,
-                                  bytes_per_column, l2_budget_bytes, d_col_hints, d_workspace, workspace_bytes,
-                                  (cudaStream_t)stream);
+int f3s_block_hints(const int32_t* d_window_offsets, const int32_t* d_block_cols, const int32_t* d_order,
+                    int32_t num_items, int32_t num_row_windows, int64_t bytes_per_column, int64_t l2_budget_bytes,
+                    uint8_t* d_block_hints, void* d_workspace, size_t workspace_bytes, f3s_stream_t stream) {
+    return f3s::block_hints_impl(d_window_offsets, d_block_cols, d_order, num_items, num_row_windows,
+                                 bytes_per_column, l2_budget_bytes, d_block_hints, d_workspace, workspace_bytes,
+                                 (cudaStream_t)stream);
 }
 
 size_t f3s_window_order_workspace_size(int32_t num_row_windows) {

@@ -23,8 +23,8 @@
 //     (chunk_row()).  The K and V boxes of a block are issued by separate
 //     lanes of the producer warp in one instruction.
 //   * L2 eviction priority per load: Q tiles (read once) evict-first; K/V
-//     tiles by the caller's per-column hint (popular columns evict-last,
-//     columns used by one window evict-first).
+//     tiles by the caller's per-block hint, the hint of the block's column
+//     (popular columns evict-last, columns used by one window evict-first).
 //   * Warp specialisation: warp 8 is the producer (ticket fetch, window
 //     metadata, block-column list read 32 at a time, TMA issue into a ring of
 //     STAGES K/V stages guarded by full/empty mbarriers); warps 0-7 consume.
@@ -80,6 +80,10 @@ struct FwdCfg {
     static constexpr int S_SUB = (STAGES_FIT > 32 ? 32 : STAGES_FIT) / SPLITS;
     static constexpr int STAGES = S_SUB * SPLITS;
     static_assert(S_SUB >= 2, "need at least two stages per split");
+    // blocks the producer issues per round (one per lane); a multiple of
+    // SPLITS that divides 32, and at most STAGES
+    static constexpr int ISSUE_W = STAGES >= 32 ? 32 : (STAGES >= 16 ? 16 : (STAGES >= 8 ? 8 : (STAGES >= 4 ? 4 : 2)));
+    static_assert(ISSUE_W % SPLITS == 0 && ISSUE_W <= STAGES, "issue width");
     static constexpr int Q_OFF = 0;
     static constexpr int KV_OFF = 2 * TILE;
     static constexpr int MERGE_OFF = KV_OFF + STAGES * 2 * TILE;
@@ -131,7 +135,7 @@ struct FwdParams {
     int q_windows;      // windows in the slab
     int q_rows;         // rows of the Q / O slab
     int tail;           // N % 16 (0: no masked column)
-    const uint8_t* hints;  // per block column L2 hint (1 keep, 2 stream, else normal) or null
+    const uint8_t* hints;  // per block L2 hint (1 keep, 2 stream, else normal) or null
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -244,47 +248,60 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         const int total = n_units * p.groups;
         const int bi = lane % C::NBOX;  // box of this lane: 0 = a (HA chunks), 1 = b (last chunk)
-        const bool vlane = lane >= C::NBOX;
-        const CUtensorMap* tkv = vlane ? (bi ? &maps.vb : &maps.va) : (bi ? &maps.kb : &maps.ka);
         const CUtensorMap* tq = bi ? &maps.qb : &maps.qa;
         const uint32_t box_off = bi ? (uint32_t)(C::HA * 2048) : 0u;  // 16 nodes x HA x 128 B
         const int box_hc = bi ? C::HA : 0;
-        const uint32_t kv_half = vlane ? (uint32_t)C::TILE : 0u;
         uint32_t cnt[C::SPLITS];  // blocks issued per split
 #pragma unroll
         for (int t = 0; t < C::SPLITS; ++t) cnt[t] = 0;
         int k = 0;        // windows published
         bool aborted = false;
-        int item = 0;
-        if (lane == 0) item = atomicAdd(&p.hdr->counter, 1);
-        item = __shfl_sync(0xffffffffu, item, 0);
+        // Work tickets run two items ahead and descriptors one ahead, and the
+        // next item's first 32 block columns (with their block hints) load
+        // while this item issues: an item's first TMA never waits on a chain
+        // of global loads.
+        auto fetch = [&](int t) -> int4 {  // (window, b0, b1, partial slot); window -1 past the end
+            if (t >= total) return make_int4(-1, 0, 0, -1);
+            const int unit = t / p.groups;
+            if (pieces != nullptr) return __ldg(pieces + unit);
+            const int wd = __ldg(p.order + unit);
+            if (wd < 0 || wd >= p.nrw_total) return make_int4(wd, 0, 0, -1);
+            return make_int4(wd, __ldg(p.offsets + wd), __ldg(p.offsets + wd + 1), -1);
+        };
+        auto first_chunk = [&](const int4& dd, int& c, int& h) {
+            const bool ok = dd.x >= 0 && dd.y >= 0 && dd.z <= b_total && dd.y + lane < dd.z;
+            c = ok ? __ldg(p.cols + dd.y + lane) : 0;
+            h = (ok && p.hints != nullptr) ? (int)__ldg(p.hints + dd.y + lane) : 0;
+        };
+        int t0 = 0, t1 = 0, t2 = 0;
+        if (lane == 0) {
+            t0 = atomicAdd(&p.hdr->counter, 1);
+            t1 = atomicAdd(&p.hdr->counter, 1);
+            t2 = atomicAdd(&p.hdr->counter, 1);
+        }
+        t0 = __shfl_sync(0xffffffffu, t0, 0);
+        t1 = __shfl_sync(0xffffffffu, t1, 0);
+        t2 = __shfl_sync(0xffffffffu, t2, 0);
+        int4 d0 = fetch(t0), d1 = fetch(t1);
+        int c0 = 0, h0 = 0;
+        first_chunk(d0, c0, h0);
         for (;;) {
-            const bool end = item >= total;
-            int w = -1, g = 0, b0 = 0, b1 = 0, pslot = -1, nxt = total;
+            const bool end = t0 >= total;
+            int w = -1, g = 0, b0 = 0, b1 = 0, pslot = -1;
+            int t3 = total;
+            int4 d2 = make_int4(-1, 0, 0, -1);
+            int c1 = 0, h1 = 0;
             if (!end) {
-                if (lane == 0) nxt = atomicAdd(&p.hdr->counter, 1);
-                const int unit = item / p.groups;
-                g = item - unit * p.groups;
-                if (pieces != nullptr) {
-                    const int4 pc = __ldg(pieces + unit);
-                    w = pc.x;
-                    b0 = pc.y;
-                    b1 = pc.z;
-                    pslot = pc.w;
-                } else {
-                    w = __ldg(p.order + unit);
-                }
-                if (w < p.q_window_base || w >= p.q_window_base + p.q_windows) {
-                    if (lane == 0) raise_error(err, F3S_ERR_BAD_FORMAT);
-                    aborted = true;
-                    break;
-                }
-                const int wb0 = __ldg(p.offsets + w), wb1 = __ldg(p.offsets + w + 1);
-                if (pieces == nullptr) {
-                    b0 = wb0;
-                    b1 = wb1;
-                }
-                if (wb0 < 0 || wb1 < wb0 || wb1 > b_total || b0 < wb0 || b1 < b0 || b1 > wb1) {
+                if (lane == 0 && t2 < total) t3 = atomicAdd(&p.hdr->counter, 1);
+                d2 = fetch(t2);
+                first_chunk(d1, c1, h1);
+                g = t0 - (t0 / p.groups) * p.groups;
+                w = d0.x;
+                b0 = d0.y;
+                b1 = d0.z;
+                pslot = d0.w;
+                if (w < p.q_window_base || w >= p.q_window_base + p.q_windows || b0 < 0 || b1 < b0 ||
+                    b1 > b_total) {
                     if (lane == 0) raise_error(err, F3S_ERR_BAD_FORMAT);
                     aborted = true;
                     break;
@@ -315,50 +332,102 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 tma_load_3d_hint(q_s + q * C::TILE + box_off, tq, qfull(q), 0, z0 + box_hc,
                                  16 * (w - p.q_window_base), pol_first);
             ++k;
-            int myc = lane < b1 - b0 ? __ldg(p.cols + b0 + lane) : 0;
+            int myc = c0, myh = h0;
             for (int base = b0; base < b1; base += 32) {
                 const int n = min(32, b1 - base);
                 // next chunk of the block list, in flight while this one issues
                 const int nbase = base + 32;
-                const int nc = nbase + lane < b1 ? __ldg(p.cols + nbase + lane) : 0;
+                const bool more = nbase + lane < b1;
+                const int nc = more ? __ldg(p.cols + nbase + lane) : 0;
+                const int nh = (more && p.hints != nullptr) ? (int)__ldg(p.hints + nbase + lane) : 0;
                 if (__any_sync(0xffffffffu, lane < n && (myc < 0 || myc >= p.nrw_total))) {
                     if (lane == 0) raise_error(err, F3S_ERR_BAD_FORMAT);
                     aborted = true;
                     break;
                 }
-                const int myh = (p.hints != nullptr && lane < n) ? (int)__ldg(p.hints + myc) : 0;
-                for (int i = 0; i < n; ++i) {
-                    const int c = __shfl_sync(0xffffffffu, myc, i);
-                    const int h = __shfl_sync(0xffffffffu, myh, i);
-                    const int bsp = (base - b0 + i) % C::SPLITS;
+                // Up to W blocks per round, one per lane: each lane claims its
+                // block's stage (split lane % SPLITS, that split's next slots
+                // in lane order) and issues the block's K and V boxes as soon
+                // as its own stage is free, so the ring stays as full as with
+                // one block at a time while the issues overlap.  W <= STAGES:
+                // no lane waits on a stage filled in the same round.
+                for (int sub = 0; sub < n; sub += C::ISSUE_W) {
+                    const int m = min(C::ISSUE_W, n - sub);
+                    const bool act = lane < m;
+                    const int c = __shfl_sync(0xffffffffu, myc, (sub + lane) & 31);
+                    const int h = __shfl_sync(0xffffffffu, myh, (sub + lane) & 31);
+                    const int bsp = lane % C::SPLITS;  // base - b0 and sub are multiples of SPLITS
                     uint32_t l = 0;
 #pragma unroll
                     for (int t = 0; t < C::SPLITS; ++t)
                         if (t == bsp) l = cnt[t];
+                    l += (uint32_t)(lane / C::SPLITS);
                     const uint32_t s = slot_of(bsp, l);
-                    if (!wait_fast(empty(s), par_of(l) ^ 1u, err, p.timeout_ns)) {
-                        aborted = true;
-                        break;
-                    }
-                    if (lane == 0) {
+                    const uint32_t par = par_of(l) ^ 1u;
+                    const uint64_t pol = h == 1 ? pol_last : (h == 2 ? pol_first : pol_normal);
+                    auto issue = [&]() {
                         stage_col[s] = c;
                         mbar_arrive_expect_tx(full(s), 2 * C::TILE);
+                        const uint32_t dst = kv_s + s * 2 * C::TILE;
+                        tma_load_3d_hint(dst, &maps.ka, full(s), 0, z0, 16 * c, pol);
+                        tma_load_3d_hint(dst + C::TILE, &maps.va, full(s), 0, z0, 16 * c, pol);
+                        if constexpr (C::NBOX == 2) {
+                            tma_load_3d_hint(dst + C::HA * 2048, &maps.kb, full(s), 0, z0 + C::HA, 16 * c, pol);
+                            tma_load_3d_hint(dst + C::TILE + C::HA * 2048, &maps.vb, full(s), 0, z0 + C::HA, 16 * c,
+                                             pol);
+                        }
+                    };
+                    bool issued = !act;
+                    if (act && mbar_try_wait(empty(s), par)) {
+                        issue();
+                        issued = true;
                     }
-                    __syncwarp();
-                    if (lane < 2 * C::NBOX) {
-                        const uint64_t pol = h == 1 ? pol_last : (h == 2 ? pol_first : pol_normal);
-                        tma_load_3d_hint(kv_s + s * 2 * C::TILE + kv_half + box_off, tkv, full(s), 0,
-                                         z0 + box_hc, 16 * c, pol);
+                    if (!__all_sync(0xffffffffu, issued)) {
+                        // bounded retry loop, uniform over the warp
+                        const uint64_t t_start = global_timer_ns();
+                        for (int spin = 1;; ++spin) {
+                            if (!issued && mbar_try_wait(empty(s), par)) {
+                                issue();
+                                issued = true;
+                            }
+                            if (__all_sync(0xffffffffu, issued)) break;
+                            if ((spin & 15) == 0) {
+                                bool stop = __any_sync(0xffffffffu, load_volatile(err.abort) != 0);
+                                if (!stop && global_timer_ns() - t_start > p.timeout_ns) {
+                                    if (lane == 0) raise_error(err, F3S_ERR_TIMEOUT);
+                                    stop = true;
+                                }
+                                if (__any_sync(0xffffffffu, stop)) {
+                                    aborted = true;
+                                    break;
+                                }
+                            }
+                        }
                     }
+                    // a split's stages free in slot order, so its issued lanes
+                    // are a prefix: the counts stay exact even on abort
+                    const uint32_t done = __ballot_sync(0xffffffffu, issued && act);
 #pragma unroll
-                    for (int t = 0; t < C::SPLITS; ++t)
-                        if (t == bsp) cnt[t] = l + 1;
+                    for (int t = 0; t < C::SPLITS; ++t) {
+                        uint32_t mask_t = 0;
+#pragma unroll
+                        for (int j = t; j < 32; j += C::SPLITS) mask_t |= 1u << j;
+                        cnt[t] += (uint32_t)__popc(done & mask_t);
+                    }
+                    if (aborted) break;
                 }
                 if (aborted) break;
                 myc = nc;
+                myh = nh;
             }
             if (aborted) break;
-            item = __shfl_sync(0xffffffffu, nxt, 0);
+            t0 = t1;
+            t1 = t2;
+            t2 = __shfl_sync(0xffffffffu, t3, 0);
+            d0 = d1;
+            d1 = d2;
+            c0 = c1;
+            h0 = h1;
         }
         if (aborted && lane == 0) {
             // let this CTA's own bulk copies land before it exits
@@ -656,39 +725,97 @@ __global__ void __launch_bounds__(256) k_plan_fill(const int* __restrict__ offse
     if (split) splits[woff[i]] = make_int4(w, soff[i], cnt, 0);
 }
 
-// One CTA per (split window, head group): O = sum_k 2^(m_k - M) O_k /
-// sum_k 2^(m_k - M) l_k over the window's pieces, in piece order.
+// One CTA per (split window, head group): O = sum_k c_k O_k with
+// c_k = 2^(m_k - M) / sum_j 2^(m_j - M) l_j over the window's pieces, summed
+// in piece order (deterministic).  Per unit: a warp per row finds M and the
+// sum (lanes over pieces); the coefficients of up to 32 pieces are staged in
+// shared memory; each thread then accumulates float4s of O with the loads of
+// consecutive pieces in flight together.
 template <int D>
 __global__ void __launch_bounds__(256) k_merge_pieces(const PlanHeader* __restrict__ ph, float* __restrict__ O,
                                                       int heads, int num_nodes, int q_window_base, int q_rows) {
+    constexpr int kMaxRows = 8 * 16;            // hg * 16 <= 128 rows of (head, node)
+    constexpr int kChunk = 32;                  // pieces per coefficient chunk
+    constexpr int kEpt = kMaxRows * D / 4 / 256 > 8 ? 8 : kMaxRows * D / 4 / 256;  // float4s per thread
+    __shared__ float s_max[kMaxRows], s_inv[kMaxRows];
+    __shared__ float s_coef[kChunk][kMaxRows];
     if (ph->status != 0 || ph->heads != heads || ph->head_dim != D) return;
     const int4* splits = reinterpret_cast<const int4*>(reinterpret_cast<const char*>(ph) + ph->splits_off);
     const float* partials = reinterpret_cast<const float*>(reinterpret_cast<const char*>(ph) + ph->partials_off);
     const int groups = ph->groups, hg = ph->hg;
-    const size_t slot_f = (size_t)hg * 16 * (D + 2);
+    const int rows = hg * 16;
+    if (rows > kMaxRows || rows * D / 4 > kEpt * 256) return;  // plans are built with hg * d <= 512
+    const size_t slot_f = (size_t)rows * (D + 2);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int unit = blockIdx.x; unit < ph->num_split * groups; unit += gridDim.x) {
-    const int sidx = unit / groups, g = unit - sidx * groups;
-    const int4 sw = splits[sidx];  // (window, first slot, pieces, -)
-    for (int e = threadIdx.x; e < hg * 16 * D; e += blockDim.x) {
-        const int hh = e / (16 * D), r = (e / D) % 16, dd = e % D;
-        const int row = 16 * sw.x + r;
-        const int64_t srow = (int64_t)row - 16 * (int64_t)q_window_base;
-        if (row >= num_nodes || srow >= q_rows) continue;
-        float M = -INFINITY;
-        for (int k = 0; k < sw.z; ++k) {
-            const float* ml = partials + ((size_t)(sw.y + k) * groups + g) * slot_f + (size_t)hg * 16 * D;
-            M = fmaxf(M, ml[hh * 32 + 2 * r]);
+        const int sidx = unit / groups, g = unit - sidx * groups;
+        const int4 sw = splits[sidx];  // (window, first slot, pieces, -)
+        const float* base = partials + ((size_t)sw.y * groups + g) * slot_f;
+        const size_t pstride = (size_t)groups * slot_f;  // floats between consecutive pieces
+        const float* ml_base = base + (size_t)rows * D;  // (m, l) pairs per row
+        for (int row = warp; row < rows; row += 8) {
+            float mx = -INFINITY;
+            for (int k = lane; k < sw.z; k += 32) mx = fmaxf(mx, __ldcs(ml_base + k * pstride + 2 * row));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            float sum = 0.f;
+            for (int k = lane; k < sw.z; k += 32) {
+                const float2 v = __ldcs(reinterpret_cast<const float2*>(ml_base + k * pstride + 2 * row));
+                sum = fmaf(fast_exp2(v.x - mx), v.y, sum);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (lane == 0) {
+                s_max[row] = mx;
+                s_inv[row] = sum > 0.f ? 1.f / sum : 0.f;
+            }
         }
-        float L = 0.f, acc = 0.f;
-        for (int k = 0; k < sw.z; ++k) {
-            const float* slot = partials + ((size_t)(sw.y + k) * groups + g) * slot_f;
-            const float* ml = slot + (size_t)hg * 16 * D + hh * 32 + 2 * r;
-            const float f = fast_exp2(ml[0] - M);
-            L = fmaf(f, ml[1], L);
-            acc = fmaf(f, slot[(size_t)hh * 16 * D + r * D + dd], acc);
+        float4 acc[kEpt];
+#pragma unroll
+        for (int e = 0; e < kEpt; ++e) acc[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int kc = 0; kc < sw.z; kc += kChunk) {
+            const int nk = min(kChunk, sw.z - kc);
+            __syncthreads();  // s_max / s_inv written; previous chunk's coefficients consumed
+            for (int i = threadIdx.x; i < nk * rows; i += 256) {
+                const int kk = i / rows, row = i - kk * rows;
+                const float m = __ldcs(ml_base + (kc + kk) * pstride + 2 * row);
+                s_coef[kk][row] = fast_exp2(m - s_max[row]) * s_inv[row];
+            }
+            __syncthreads();
+#pragma unroll
+            for (int e = 0; e < kEpt; ++e) {
+                const int idx = threadIdx.x + e * 256;
+                if (idx < rows * D / 4) {
+                    const int row = idx / (D / 4);
+                    const float4* src = reinterpret_cast<const float4*>(base + (size_t)kc * pstride) + idx;
+                    const size_t step4 = pstride / 4;
+                    float4 a = acc[e];
+#pragma unroll 4
+                    for (int kk = 0; kk < nk; ++kk) {
+                        const float4 v = __ldcs(src + kk * step4);
+                        const float c = s_coef[kk][row];
+                        a.x = fmaf(c, v.x, a.x);
+                        a.y = fmaf(c, v.y, a.y);
+                        a.z = fmaf(c, v.z, a.z);
+                        a.w = fmaf(c, v.w, a.w);
+                    }
+                    acc[e] = a;
+                }
+            }
         }
-        O[(srow * heads + (int64_t)g * hg + hh) * D + dd] = L > 0.f ? acc / L : 0.f;
-    }
+#pragma unroll
+        for (int e = 0; e < kEpt; ++e) {
+            const int idx = threadIdx.x + e * 256;
+            if (idx < rows * D / 4) {
+                const int row = idx / (D / 4), c4 = idx - row * (D / 4);
+                const int hh = row >> 4, r = row & 15;
+                const int node = 16 * sw.x + r;
+                const int64_t srow = (int64_t)node - 16 * (int64_t)q_window_base;
+                if (node < num_nodes && srow < q_rows)
+                    __stcs(reinterpret_cast<float4*>(O + (srow * heads + (int64_t)g * hg + hh) * D) + c4, acc[e]);
+            }
+        }
+        __syncthreads();  // s_max / s_inv reused by the next unit
     }
 }
 
@@ -856,7 +983,7 @@ int make_plan_impl(const int* offsets, const int* order, int num_items, int64_t 
 }
 
 int forward_impl(const void* Q, const void* K, const void* V, float* O, const int* offsets, const int* cols,
-                 const int* order, const uint8_t* col_hints, const void* plan, int num_items, int num_nodes,
+                 const int* order, const uint8_t* block_hints, const void* plan, int num_items, int num_nodes,
                  int heads, int head_dim, int q_window_base, int q_rows, void* ws, size_t ws_bytes,
                  cudaStream_t stream, uint64_t timeout_ns) {
     if (num_items < 0 || num_nodes < 0 || heads <= 0 || q_window_base < 0 || q_rows < 0)
@@ -877,7 +1004,7 @@ int forward_impl(const void* Q, const void* K, const void* V, float* O, const in
     prm.cols = cols;
     prm.order = order;
     prm.plan = static_cast<PlanHeader*>(const_cast<void*>(plan));
-    prm.hints = col_hints;
+    prm.hints = block_hints;
     prm.hdr = static_cast<WsHeader*>(ws);
     prm.timeout_ns = timeout_ns;
     prm.num_items = num_items;
@@ -955,10 +1082,10 @@ int f3s_make_plan(const int32_t* d_window_offsets, const int32_t* d_order, int32
 }
 
 int f3s_forward(const void* d_Q, const void* d_K, const void* d_V, float* d_O, const int32_t* d_window_offsets,
-                const int32_t* d_block_cols, const int32_t* d_order, const uint8_t* d_col_hints, const void* d_plan,
+                const int32_t* d_block_cols, const int32_t* d_order, const uint8_t* d_block_hints, const void* d_plan,
                 int32_t num_items, int32_t num_nodes, int32_t heads, int32_t head_dim, int32_t q_window_base,
                 int32_t q_rows, void* d_workspace, size_t workspace_bytes, f3s_stream_t stream) {
-    return f3s::forward_impl(d_Q, d_K, d_V, d_O, d_window_offsets, d_block_cols, d_order, d_col_hints, d_plan,
+    return f3s::forward_impl(d_Q, d_K, d_V, d_O, d_window_offsets, d_block_cols, d_order, d_block_hints, d_plan,
                              num_items, num_nodes, heads, head_dim, q_window_base, q_rows, d_workspace,
                              workspace_bytes, (cudaStream_t)stream, f3s::kWaitTimeoutNs);
 }

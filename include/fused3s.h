@@ -151,8 +151,9 @@ int f3s_window_order(const int32_t* d_window_offsets, int32_t num_row_windows, i
  *   d_window_offsets / d_block_cols: the converter's output for all windows
  *   d_order  int32[num_items] window ids to compute (any subset, any order;
  *            each must lie in [q_window_base, q_window_base + ceil(q_rows/16)))
- *   d_col_hints optional uint8[nrw] per block column L2 eviction hint from
- *            f3s_column_hints (NULL: no hint); affects speed only.
+ *   d_block_hints optional uint8[num_blocks] L2 eviction hint of every
+ *            active block from f3s_block_hints (NULL: no hint); affects
+ *            speed only.
  *   d_plan   optional plan from f3s_make_plan (NULL: one work item per entry
  *            of d_order).  With a plan, d_order / num_items are not used: the
  *            plan lists the windows, heavy ones cut into pieces.
@@ -165,7 +166,7 @@ int f3s_window_order(const int32_t* d_window_offsets, int32_t num_row_windows, i
 size_t f3s_forward_workspace_size(void);
 int f3s_forward(const void* d_Q, const void* d_K, const void* d_V, float* d_O,
                 const int32_t* d_window_offsets, const int32_t* d_block_cols, const int32_t* d_order,
-                const uint8_t* d_col_hints, const void* d_plan, int32_t num_items, int32_t num_nodes,
+                const uint8_t* d_block_hints, const void* d_plan, int32_t num_items, int32_t num_nodes,
                 int32_t heads, int32_t head_dim, int32_t q_window_base, int32_t q_rows, void* d_workspace,
                 size_t workspace_bytes, f3s_stream_t stream);
 
@@ -190,20 +191,23 @@ int f3s_make_plan(const int32_t* d_window_offsets, const int32_t* d_order, int32
                   void* d_plan, size_t plan_bytes, f3s_stream_t stream);
 
 /* ------------------------------------------------------------------------
- * Per block column L2 eviction hints for f3s_forward (no reference
+ * L2 eviction hints for f3s_forward, one per active block (no reference
  * counterpart: a speed hint computed once per graph and window set).
  *
  * Counts, for the windows listed in d_order[0 .. num_items), how many of
  * them reference each block column; the most popular columns whose K/V
  * bytes (bytes_per_column = 16 * heads * head_dim * 2 * 2) fit in
- * l2_budget_bytes get hint 1 (keep: evict-last), columns referenced once get
- * hint 2 (stream: evict-first), the rest 0.  d_col_hints: uint8[nrw].
+ * l2_budget_bytes get hint 1 (keep: evict-last), columns referenced by one
+ * listed window get hint 2 (stream: evict-first), the rest 0.  Every block
+ * gets its column's hint, so the forward reads it next to the block's
+ * column index.  d_block_hints: uint8[d_window_offsets[num_row_windows]]
+ * (entries of unlisted windows' blocks are written but not meaningful).
  * ---------------------------------------------------------------------- */
-size_t f3s_column_hints_workspace_size(int32_t num_row_windows);
-int f3s_column_hints(const int32_t* d_window_offsets, const int32_t* d_block_cols, const int32_t* d_order,
-                     int32_t num_items, int32_t num_row_windows, int64_t bytes_per_column,
-                     int64_t l2_budget_bytes, uint8_t* d_col_hints, void* d_workspace,
-                     size_t workspace_bytes, f3s_stream_t stream);
+size_t f3s_block_hints_workspace_size(int32_t num_row_windows);
+int f3s_block_hints(const int32_t* d_window_offsets, const int32_t* d_block_cols, const int32_t* d_order,
+                    int32_t num_items, int32_t num_row_windows, int64_t bytes_per_column,
+                    int64_t l2_budget_bytes, uint8_t* d_block_hints, void* d_workspace,
+                    size_t workspace_bytes, f3s_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Drop-in launch with the reference kernel's exact argument list

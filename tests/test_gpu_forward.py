@@ -210,24 +210,39 @@ def test_float2half_matches_torch(lib):
     assert torch.equal(F.float2half(x), x.half())
 
 
-def test_column_hints_only_change_speed(lib):
-    """L2 hints are valid (0/1/2), mark single-use columns as streamed, and
-    leave the output bit-identical."""
+def test_block_hints_only_change_speed(lib):
+    """L2 hints are one per block and valid (0/1/2): a block's hint is its
+    column's, single-use columns are streamed, kept columns are the most
+    popular; the output is bit-identical with and without hints."""
     g = G.rmat_graph(14, 16, device="cuda", name="rmat14")
     q, k, v = features_np(g.num_nodes, 8, 64, "normal")
     fmt = F.convert_csr_to_block_sparse(g.num_nodes, g.row_ptr, g.col_ind)
     Q, K, V = to_gpu(q, k, v)
-    hints = F.column_hints(fmt, 8, 64, l2_fraction=0.001)
+    hints = F.block_hints(fmt, 8, 64, l2_fraction=0.001)
     h = hints.cpu().numpy()
-    assert set(np.unique(h)) <= {0, 1, 2}
     off, cols = fmt.to_host()
+    assert h.shape == cols.shape
+    assert set(np.unique(h)) <= {0, 1, 2}
     pop = np.bincount(cols, minlength=fmt.num_row_windows)
-    assert np.all(h[pop == 1] == 2)
+    # one hint per column: every block of a column carries the same value
+    col_hint = np.full(fmt.num_row_windows, 255, np.int64)
+    col_hint[cols] = h
+    assert np.array_equal(col_hint[cols], h)
+    assert np.all(h[pop[cols] == 1] == 2)
     if (h == 1).any():
-        assert pop[h == 1].min() >= pop[h == 0].max(initial=0)
+        assert pop[cols][h == 1].min() >= pop[cols][h == 0].max(initial=0)
+        assert pop[cols][h == 1].min() >= 2
     a = F.fused3s_forward(Q, K, V, fmt, check_status=True).cpu()
-    b = F.fused3s_forward(Q, K, V, fmt, col_hints=hints, check_status=True).cpu()
+    b = F.fused3s_forward(Q, K, V, fmt, block_hints=hints, check_status=True).cpu()
     assert torch.equal(a, b)
+    # a subset of windows: blocks of listed windows count only listed windows
+    order = torch.arange(0, fmt.num_row_windows, 3, dtype=torch.int32, device="cuda")
+    hs = F.block_hints(fmt, 8, 64, order=order, l2_fraction=0.001).cpu().numpy()
+    listed = np.zeros(fmt.num_row_windows, bool)
+    listed[order.cpu().numpy()] = True
+    in_listed = np.repeat(listed, np.diff(off))
+    pop_s = np.bincount(cols[in_listed], minlength=fmt.num_row_windows)
+    assert np.all(hs[in_listed & (pop_s[cols] == 1)] == 2)
 
 
 @pytest.mark.parametrize("heads,head_dim", [(1, 64), (2, 128), (4, 128)])
