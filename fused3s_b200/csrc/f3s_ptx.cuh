@@ -69,7 +69,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // give up when another thread has raised the abort flag, or after
 // `timeout_ns` of global time (then raise F3S_ERR_TIMEOUT).  Returns false on
 // give-up.  The result is made warp-uniform by the caller where needed.
-static __device__ __noinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, const ErrorSink& e,
+static __device__ __noinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, const ErrorSink e,
                                                uint64_t timeout_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();

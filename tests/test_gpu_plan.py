@@ -96,3 +96,40 @@ def test_plan_overflow_is_reported(lib):
         F.fused3s_forward(q, k, v, fmt, plan=plan, check_status=True)
     assert e.value.status == _lib.F3S_ERR_BAD_FORMAT
     F.fused3s_forward(q, k, v, fmt, check_status=True)  # device still fine
+
+
+def test_plan_usable_after_failed_forward(lib):
+    """A planned forward that aborts (here: plan windows outside the Q slab)
+    is reported, and the same plan then gives the exact result."""
+    g = G.powerlaw_graph(num_nodes=2003, directed_edges=20000, max_degree=500, seed=21)
+    q, k, v = feats(g.num_nodes, 2, 64)
+    fmt = F.convert_csr_to_block_sparse(g.num_nodes, g.row_ptr, g.col_ind)
+    Q, K, V = gpu(q, k, v)
+    plan = F.make_plan(fmt, 2, 64, max_blocks=4)
+    with pytest.raises(_lib.Fused3SError) as e:
+        F.fused3s_forward(Q[:160].contiguous(), K, V, fmt, plan=plan, check_status=True)
+    assert e.value.status == _lib.F3S_ERR_BAD_FORMAT
+    o = F.fused3s_forward(Q, K, V, fmt, plan=plan, check_status=True).cpu().numpy()
+    off, cols = fmt.to_host()
+    ref = oracle.block_attention(g.num_nodes, q.astype(np.float32), k.astype(np.float32), v.astype(np.float32),
+                                 off, cols, threads=8)
+    parity(o, ref, "plan after a failed forward")
+
+
+def test_plan_many_pieces_per_window(lib):
+    """Windows cut into hundreds of pieces (T = 1): the last-arriving piece
+    merges them all, for both head dims."""
+    for heads, head_dim in ((1, 64), (4, 128)):
+        g = G.powerlaw_graph(num_nodes=3001, directed_edges=40000, max_degree=1500, seed=5 + heads)
+        q, k, v = feats(g.num_nodes, heads, head_dim)
+        fmt = F.convert_csr_to_block_sparse(g.num_nodes, g.row_ptr, g.col_ind)
+        off, cols = fmt.to_host()
+        assert np.diff(off).max() > 100
+        Q, K, V = gpu(q, k, v)
+        plan = F.make_plan(fmt, heads, head_dim, max_blocks=1)
+        o = F.fused3s_forward(Q, K, V, fmt, plan=plan, check_status=True).cpu().numpy()
+        ref = oracle.block_attention(g.num_nodes, q.astype(np.float32), k.astype(np.float32),
+                                     v.astype(np.float32), off, cols, threads=8)
+        parity(o, ref, f"T=1 H={heads} d={head_dim}")
+        o2 = F.fused3s_forward(Q, K, V, fmt, plan=plan, check_status=True).cpu().numpy()
+        assert np.array_equal(o, o2)
