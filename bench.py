@@ -175,11 +175,12 @@ def make_features_device(n, h, d, kind, seed, device):
     return out
 
 
-def alg_bytes(heads, d, B, nrw):
+def alg_bytes(heads, d, B, nrw, o_bytes=4):
     """Algorithmic HBM bytes of one forward: per head, K and V tiles of every
-    active block (64*d B), the Q tile (32*d B) and fp32 O tile (64*d B) of
-    every window; plus the block-column list and window offsets."""
-    return heads * (64 * d * B + 96 * d * nrw) + 4 * B + 8 * nrw
+    active block (64*d B), the Q tile (32*d B) and O tile (16*d*o_bytes B:
+    64*d for fp32 O) of every window; plus the block-column list and window
+    offsets."""
+    return heads * (64 * d * B + (32 + 16 * o_bytes) * d * nrw) + 4 * B + 8 * nrw
 
 
 def alg_flops(heads, d, B):
@@ -314,7 +315,9 @@ def run_ours(args):
     Qf, Kf, Vf = make_features_device(N, H, d, cfg.features, 42, dev)
     Q = Qf[r0:r1].contiguous()
     del Qf
-    O = torch.empty((r1 - r0, H, d), dtype=torch.float32, device=dev)
+    o_torch = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[args.out_dtype]
+    o_code = {"f32": _lib.F3S_OUT_F32, "f16": _lib.F3S_OUT_F16, "bf16": _lib.F3S_OUT_BF16}[args.out_dtype]
+    O = torch.empty((r1 - r0, H, d), dtype=o_torch, device=dev)
     ws = F.forward_workspace(dev)
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
@@ -345,12 +348,12 @@ def run_ours(args):
     def step():
         # launches on the current stream (the capture stream while a graph
         # is being recorded)
-        st = lib.f3s_forward(Q.data_ptr(), Kf.data_ptr(), Vf.data_ptr(), O.data_ptr(),
-                             fmt.window_offsets.data_ptr(), fmt.cols_ptr, my_order.data_ptr(), hints_ptr,
-                             plan_ptr, n_items, N, H, d, lo, r1 - r0, ws.data_ptr(), ws.numel(),
-                             torch.cuda.current_stream(dev).cuda_stream)
+        st = lib.f3s_forward_ex(Q.data_ptr(), Kf.data_ptr(), Vf.data_ptr(), O.data_ptr(), o_code,
+                                fmt.window_offsets.data_ptr(), fmt.cols_ptr, my_order.data_ptr(), hints_ptr,
+                                plan_ptr, n_items, N, H, d, lo, r1 - r0, ws.data_ptr(), ws.numel(),
+                                torch.cuda.current_stream(dev).cuda_stream)
         if st != 0:
-            raise _lib.Fused3SError(st, "f3s_forward")
+            raise _lib.Fused3SError(st, "f3s_forward_ex")
 
     for _ in range(args.warmup):
         step()
@@ -406,12 +409,12 @@ def run_ours(args):
     # O -> pinned host, every step
     e2e = None
     h2d = (Q.numel() + Kf.numel() + Vf.numel()) * 2
-    d2h = O.numel() * 4
+    d2h = O.numel() * O.element_size()
     if not args.no_e2e and h2d + d2h < 8e9:
         hQ = Q.cpu().pin_memory()
         hK = Kf.cpu().pin_memory()
         hV = Vf.cpu().pin_memory()
-        hO = torch.empty(O.shape, dtype=torch.float32).pin_memory()
+        hO = torch.empty(O.shape, dtype=O.dtype).pin_memory()
         dQ, dK, dV = torch.empty_like(Q), torch.empty_like(Kf), torch.empty_like(Vf)
 
         def e2e_step():
@@ -444,11 +447,15 @@ def run_ours(args):
                "note": "per rank: pinned host Q slab + K + V -> device, fused forward, O slab -> host"}
         del hQ, hK, hV, hO, dQ, dK, dV
 
-    # optional all-gather of O (only when the full output is needed on every rank)
+    # optional all-gather of O (only when the full output is needed on every
+    # rank): (1) after the forward, one padded all-gather; (2) the forward in
+    # --sub-slabs launches, each sub-slab's all-gather overlapping the next
+    # launch (shard.sharded_forward_allgather)
     gather_ms = None
+    overlap_ms = None
     if world > 1 and args.gather:
         slabs = [shard.slab_rows(a, b, N) for a, b in parts]
-        ge = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        ge = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
         shard.gather_rows(O, slabs)
         dist.barrier()
         torch.cuda.synchronize()
@@ -458,12 +465,37 @@ def run_ours(args):
         torch.cuda.synchronize()
         gather_ms = ge[0].elapsed_time(ge[1])
         del full_o
+        subs = shard.sub_ranges(off_h, lo, hi, args.sub_slabs)
+        sub_plans = None
+        if plan is not None:
+            sub_plans = [F.make_plan(fmt, H, d, order=shard.rank_order(order, a, b).contiguous(), max_blocks=T)
+                         for a, b in subs]
+        og = shard.OverlappedGather(off_h, parts, rank, N, (H, d), O.dtype, dev, args.sub_slabs)
+
+        def fwd_gather():
+            return shard.sharded_forward_allgather(Q, Kf, Vf, fmt, order, parts, rank, window_offsets=off_h,
+                                                   sub_slabs=args.sub_slabs, out_dtype=O.dtype, block_hints=hints,
+                                                   plans=sub_plans, gather=og)
+
+        for _ in range(2):
+            fwd_gather()
+        dist.barrier()
+        torch.cuda.synchronize()
+        ge[2].record(stream)
+        for _ in range(args.steps):
+            fwd_gather()
+        ge[3].record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([ge[2].elapsed_time(ge[3]) / args.steps], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        overlap_ms = float(t.item())
+        del og
 
     # roofline of the fused kernel (per launch, this rank's share)
     my_blocks = int((off_h[1:] - off_h[:-1])[lo:hi].sum())
     my_windows = hi - lo
     kern_ms = statistics.median(per_step)
-    bytes_launch = alg_bytes(H, d, my_blocks, my_windows)
+    bytes_launch = alg_bytes(H, d, my_blocks, my_windows, O.element_size())
     flops_launch = alg_flops(H, d, my_blocks)
     hbm_peak, tc_peak, peak_kind = measured_peaks()
     achieved = bytes_launch / (kern_ms / 1e3) / 1e9
@@ -491,7 +523,7 @@ def run_ours(args):
                        "parallelism": f"row-window shards x{world}, K/V replicated",
                        "l2": "inputs larger than L2" if (Kf.numel() + Vf.numel()) * 2 > 126e6 else
                              "inputs fit in L2 (no flush)",
-                       "convert_ms": convert_ms, "order_ms": order_ms, "l2_hints": args.l2_hints, "cuda_graph": args.graph,
+                       "convert_ms": convert_ms, "order_ms": order_ms, "l2_hints": args.l2_hints, "cuda_graph": args.graph, "o_dtype": args.out_dtype,
                        "hints_ms": hints_ms, "split": args.split,
                        "piece_blocks": plan.max_blocks if plan is not None else None, "plan_ms": plan_ms},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
@@ -506,6 +538,9 @@ def run_ours(args):
         }
         if gather_ms is not None:
             result["allgather_o_ms"] = gather_ms
+            result["forward_then_allgather_ms"] = ms_per_step + gather_ms
+            result["forward_allgather_overlapped_ms"] = overlap_ms
+            result["sub_slabs"] = args.sub_slabs
         emit(result)
     if world > 1:
         dist.barrier()
@@ -521,6 +556,9 @@ def main(argv=None):
     ap.add_argument("--config", default="c4", choices=["c1", "c2", "c3", "c4", "c5", "c4s"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gather", action="store_true", help="also time the NCCL all-gather of O (N > 1)")
+    ap.add_argument("--sub-slabs", type=int, default=4,
+                    help="sub-slabs per rank for the overlapped forward + all-gather (--gather)")
+    ap.add_argument("--out-dtype", default="f32", choices=["f32", "f16", "bf16"], help="element type of O")
     ap.add_argument("--graph", default="on", choices=["on", "off"],
                     help="replay the timed step as a CUDA graph")
     ap.add_argument("--split", default="auto",

@@ -22,6 +22,10 @@ F3S_ERR_TIMEOUT = 6
 F3S_ERR_BAD_FORMAT = 7
 F3S_ERR_TOO_LARGE = 8
 
+F3S_OUT_F32 = 0
+F3S_OUT_F16 = 1
+F3S_OUT_BF16 = 2
+
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
 _I64 = ctypes.c_int64
@@ -42,6 +46,8 @@ SIGNATURES = {
     "f3s_forward_workspace_size": (_SZ, []),
     "f3s_forward": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P,
                                    _SZ, _P]),
+    "f3s_forward_ex": (ctypes.c_int, [_P, _P, _P, _P, _I32, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
+                                      _P, _SZ, _P]),
     "f3s_plan_size": (_SZ, [_I32, _I64, _I32, _I32, _I32]),
     "f3s_make_plan": (ctypes.c_int, [_P, _P, _I32, _I64, _I32, _I32, _I32, _P, _SZ, _P]),
     "f3s_block_hints_workspace_size": (_SZ, [_I32]),

@@ -266,10 +266,15 @@ def make_plan(fmt: BlockSparseFormat, heads: int, head_dim: int, order: Optional
     return ForwardPlan(buf, heads, head_dim, int(max_blocks))
 
 
+_OUT_DTYPES = {torch.float32: _lib.F3S_OUT_F32, torch.float16: _lib.F3S_OUT_F16,
+               torch.bfloat16: _lib.F3S_OUT_BF16}
+
+
 def fused3s_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: BlockSparseFormat,
                     order: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
                     q_window_base: int = 0, check_status: bool = False,
-                    block_hints: Optional[torch.Tensor] = None, plan: Optional[ForwardPlan] = None) -> torch.Tensor:
+                    block_hints: Optional[torch.Tensor] = None, plan: Optional[ForwardPlan] = None,
+                    out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
     """O = block-sparse softmax(Q K^T) V, fused (the fused3s_v2 path).
 
     Q: fp16 [q_rows, H, d] (or [q_rows, d] for one head) holding rows
@@ -280,7 +285,9 @@ def fused3s_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: Bloc
     check_status: synchronise and raise if a kernel recorded an error.
     block_hints: optional uint8[num_blocks] from block_hints() (speed only).
     plan: optional ForwardPlan from make_plan(); it then lists the windows
-       (order is ignored) and heavy windows run as several pieces."""
+       (order is ignored) and heavy windows run as several pieces.
+    out_dtype: element type of O when `out` is not given: float32 (as
+       computed), or float16 / bfloat16 (the fp32 result rounded to nearest)."""
     if plan is not None and (plan.heads, plan.head_dim) != (_as_nhd(Q).shape[1], _as_nhd(Q).shape[2]):
         raise ValueError("plan was made for other heads / head_dim")
     if block_hints is not None and (block_hints.dtype != torch.uint8 or block_hints.numel() < fmt.num_blocks):
@@ -305,16 +312,18 @@ def fused3s_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: Bloc
                                  device=device)
     order = order.to(device=device, dtype=torch.int32).contiguous()
     if out is None:
-        out = torch.empty(Q.shape, dtype=torch.float32, device=device)
-    elif out.dtype != torch.float32 or out.shape != Q.shape or not out.is_contiguous():
-        raise ValueError("out must be a contiguous float32 tensor shaped like Q")
+        out = torch.empty(Q.shape, dtype=out_dtype, device=device)
+    elif out.shape != Q.shape or not out.is_contiguous():
+        raise ValueError("out must be a contiguous tensor shaped like Q")
+    if out.dtype not in _OUT_DTYPES:
+        raise ValueError("O must be float32, float16 or bfloat16")
     ws = _WS.get(device, "forward", lib.f3s_forward_workspace_size())
     with torch.cuda.device(device):
-        st = lib.f3s_forward(_ptr(Q), _ptr(K), _ptr(V), _ptr(out), _ptr(fmt.window_offsets),
-                             fmt.cols_ptr, _ptr(order), _ptr(block_hints), None if plan is None else _ptr(plan.buffer),
-                             int(order.numel()), num_nodes, heads,
-                             head_dim, q_window_base, q_rows, _ptr(ws), ws.numel(), _stream_ptr(device))
-        check(st, "f3s_forward")
+        st = lib.f3s_forward_ex(_ptr(Q), _ptr(K), _ptr(V), _ptr(out), _OUT_DTYPES[out.dtype],
+                                _ptr(fmt.window_offsets), fmt.cols_ptr, _ptr(order), _ptr(block_hints),
+                                None if plan is None else _ptr(plan.buffer), int(order.numel()), num_nodes, heads,
+                                head_dim, q_window_base, q_rows, _ptr(ws), ws.numel(), _stream_ptr(device))
+        check(st, "f3s_forward_ex")
         if check_status:
             check(lib.f3s_workspace_status(_ptr(ws), _stream_ptr(device)), "f3s_forward (device)")
     return out

@@ -21,9 +21,9 @@ int num_sms_of_current_device() {
     return n;
 }
 
-int forward_impl(const void* Q, const void* K, const void* V, float* O, const int* offsets, const int* cols,
-                 const int* order, const uint8_t* block_hints, const void* plan, int num_items, int num_nodes,
-                 int heads, int head_dim, int q_window_base, int q_rows, void* ws, size_t ws_bytes,
+int forward_impl(const void* Q, const void* K, const void* V, void* O, int o_dtype, const int* offsets,
+                 const int* cols, const int* order, const uint8_t* block_hints, const void* plan, int num_items,
+                 int num_nodes, int heads, int head_dim, int q_window_base, int q_rows, void* ws, size_t ws_bytes,
                  cudaStream_t stream, uint64_t timeout_ns);
 
 // Library-owned forward workspace for the reference-signature launch, one
@@ -109,9 +109,9 @@ int f3s_1tb1rw_launch(const void* Q, const void* K, const void* V, float* O_out,
     void* ws = f3s::legacy_workspace(&rc);
     if (!ws) return rc;
     const int rows = num_row_windows * 16;
-    return f3s::forward_impl(Q, K, V, O_out, window_offsets, block_col_indices, window_order, nullptr, nullptr,
-                             num_row_windows, rows, 1, feat_dim, 0, rows, ws, f3s::kWsHeaderBytes, (cudaStream_t)stream,
-                             10ull * 1000 * 1000 * 1000);
+    return f3s::forward_impl(Q, K, V, O_out, F3S_OUT_F32, window_offsets, block_col_indices, window_order, nullptr,
+                             nullptr, num_row_windows, rows, 1, feat_dim, 0, rows, ws, f3s::kWsHeaderBytes,
+                             (cudaStream_t)stream, 10ull * 1000 * 1000 * 1000);
 }
 
 int f3s_half_from_float(const float* d_in, void* d_out, int64_t n, f3s_stream_t stream) {

@@ -44,6 +44,7 @@
 #include <algorithm>
 #include <mutex>
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 #include "f3s_internal.cuh"
 
@@ -119,7 +120,7 @@ struct PlanHeader {
 static_assert(sizeof(PlanHeader) == 256, "plan header is 256 bytes");
 
 struct FwdParams {
-    float* O;
+    void* O;            // [q_rows, H, D] of o_dtype
     const int* offsets;
     const int* cols;
     const int* order;
@@ -136,7 +137,41 @@ struct FwdParams {
     int q_rows;         // rows of the Q / O slab
     int tail;           // N % 16 (0: no masked column)
     const uint8_t* hints;  // per block L2 hint (1 keep, 2 stream, else normal) or null
+    int o_dtype;           // f3s_out_dtype of O
 };
+
+// O stores: fp32 as computed, or rounded to nearest into fp16 / bf16.
+// Streaming stores (O is written once).  idx is an element index; pairs
+// start at even, quads at multiples of 4 (aligned for every type).
+__device__ __forceinline__ void store_o2(void* O, int64_t idx, float a, float b, int dt) {
+    if (dt == F3S_OUT_F16) {
+        const __half2 v = __floats2half2_rn(a, b);
+        __stcs(reinterpret_cast<unsigned int*>(static_cast<__half*>(O) + idx), *reinterpret_cast<const unsigned int*>(&v));
+    } else if (dt == F3S_OUT_BF16) {
+        const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+        __stcs(reinterpret_cast<unsigned int*>(static_cast<__nv_bfloat16*>(O) + idx),
+               *reinterpret_cast<const unsigned int*>(&v));
+    } else {
+        __stcs(reinterpret_cast<float2*>(static_cast<float*>(O) + idx), make_float2(a, b));
+    }
+}
+
+__device__ __forceinline__ void store_o4(void* O, int64_t idx, float4 v, int dt) {
+    if (dt == F3S_OUT_F32) {
+        __stcs(reinterpret_cast<float4*>(static_cast<float*>(O) + idx), v);
+        return;
+    }
+    uint2 w;
+    if (dt == F3S_OUT_F16) {
+        const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+        w = make_uint2(*reinterpret_cast<const unsigned int*>(&a), *reinterpret_cast<const unsigned int*>(&b));
+        __stcs(reinterpret_cast<uint2*>(static_cast<__half*>(O) + idx), w);
+    } else {
+        const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+        w = make_uint2(*reinterpret_cast<const unsigned int*>(&a), *reinterpret_cast<const unsigned int*>(&b));
+        __stcs(reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(O) + idx), w);
+    }
+}
 
 __device__ __forceinline__ float fast_exp2(float x) {
     float y;
@@ -664,16 +699,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int ra = 16 * w + g4, rb = ra + 8;
         const int64_t sa = (int64_t)(ra - 16 * p.q_window_base), sb = sa + 8;
         if (ra < p.num_nodes && sa < p.q_rows) {
-            float* dst = p.O + (sa * p.heads + h) * D + 2 * t4;
+            const int64_t dst = (sa * p.heads + h) * D + 2 * t4;
 #pragma unroll
-            for (int jn = 0; jn < NT; ++jn)
-                __stcs(reinterpret_cast<float2*>(dst + jn * 8), make_float2(o[jn][0] * inv0, o[jn][1] * inv0));
+            for (int jn = 0; jn < NT; ++jn) store_o2(p.O, dst + jn * 8, o[jn][0] * inv0, o[jn][1] * inv0, p.o_dtype);
         }
         if (rb < p.num_nodes && sb < p.q_rows) {
-            float* dst = p.O + (sb * p.heads + h) * D + 2 * t4;
+            const int64_t dst = (sb * p.heads + h) * D + 2 * t4;
 #pragma unroll
-            for (int jn = 0; jn < NT; ++jn)
-                __stcs(reinterpret_cast<float2*>(dst + jn * 8), make_float2(o[jn][2] * inv1, o[jn][3] * inv1));
+            for (int jn = 0; jn < NT; ++jn) store_o2(p.O, dst + jn * 8, o[jn][2] * inv1, o[jn][3] * inv1, p.o_dtype);
         }
     }
 }
@@ -732,8 +765,9 @@ __global__ void __launch_bounds__(256) k_plan_fill(const int* __restrict__ offse
 // shared memory; each thread then accumulates float4s of O with the loads of
 // consecutive pieces in flight together.
 template <int D>
-__global__ void __launch_bounds__(256) k_merge_pieces(const PlanHeader* __restrict__ ph, float* __restrict__ O,
-                                                      int heads, int num_nodes, int q_window_base, int q_rows) {
+__global__ void __launch_bounds__(256) k_merge_pieces(const PlanHeader* __restrict__ ph, void* __restrict__ O,
+                                                      int heads, int num_nodes, int q_window_base, int q_rows,
+                                                      int o_dtype) {
     constexpr int kMaxRows = 8 * 16;            // hg * 16 <= 128 rows of (head, node)
     constexpr int kChunk = 32;                  // pieces per coefficient chunk
     constexpr int kEpt = kMaxRows * D / 4 / 256 > 8 ? 8 : kMaxRows * D / 4 / 256;  // float4s per thread
@@ -812,7 +846,7 @@ __global__ void __launch_bounds__(256) k_merge_pieces(const PlanHeader* __restri
                 const int node = 16 * sw.x + r;
                 const int64_t srow = (int64_t)node - 16 * (int64_t)q_window_base;
                 if (node < num_nodes && srow < q_rows)
-                    __stcs(reinterpret_cast<float4*>(O + (srow * heads + (int64_t)g * hg + hh) * D) + c4, acc[e]);
+                    store_o4(O, (srow * heads + (int64_t)g * hg + hh) * D + 4 * c4, acc[e], o_dtype);
             }
         }
         __syncthreads();  // s_max / s_inv reused by the next unit
@@ -927,7 +961,7 @@ static int launch_variant(const void* Q, const void* K, const void* V, FwdParams
     F3S_LAUNCH_CHECK();
     if (prm.plan) {
         k_merge_pieces<D><<<2 * sms, 256, 0, stream>>>(prm.plan, prm.O, prm.heads, prm.num_nodes, prm.q_window_base,
-                                                       prm.q_rows);
+                                                       prm.q_rows, prm.o_dtype);
         F3S_LAUNCH_CHECK();
     }
     return F3S_SUCCESS;
@@ -982,10 +1016,11 @@ int make_plan_impl(const int* offsets, const int* order, int num_items, int64_t 
     return F3S_SUCCESS;
 }
 
-int forward_impl(const void* Q, const void* K, const void* V, float* O, const int* offsets, const int* cols,
-                 const int* order, const uint8_t* block_hints, const void* plan, int num_items, int num_nodes,
-                 int heads, int head_dim, int q_window_base, int q_rows, void* ws, size_t ws_bytes,
+int forward_impl(const void* Q, const void* K, const void* V, void* O, int o_dtype, const int* offsets,
+                 const int* cols, const int* order, const uint8_t* block_hints, const void* plan, int num_items,
+                 int num_nodes, int heads, int head_dim, int q_window_base, int q_rows, void* ws, size_t ws_bytes,
                  cudaStream_t stream, uint64_t timeout_ns) {
+    if (o_dtype != F3S_OUT_F32 && o_dtype != F3S_OUT_F16 && o_dtype != F3S_OUT_BF16) return F3S_ERR_INVALID_VALUE;
     if (num_items < 0 || num_nodes < 0 || heads <= 0 || q_window_base < 0 || q_rows < 0)
         return F3S_ERR_INVALID_VALUE;
     if (head_dim != 64 && head_dim != 128) return F3S_ERR_UNSUPPORTED;
@@ -1000,6 +1035,7 @@ int forward_impl(const void* Q, const void* K, const void* V, float* O, const in
     const int hg = pick_head_group(heads, head_dim);
     FwdParams prm{};
     prm.O = O;
+    prm.o_dtype = o_dtype;
     prm.offsets = offsets;
     prm.cols = cols;
     prm.order = order;
@@ -1085,8 +1121,18 @@ int f3s_forward(const void* d_Q, const void* d_K, const void* d_V, float* d_O, c
                 const int32_t* d_block_cols, const int32_t* d_order, const uint8_t* d_block_hints, const void* d_plan,
                 int32_t num_items, int32_t num_nodes, int32_t heads, int32_t head_dim, int32_t q_window_base,
                 int32_t q_rows, void* d_workspace, size_t workspace_bytes, f3s_stream_t stream) {
-    return f3s::forward_impl(d_Q, d_K, d_V, d_O, d_window_offsets, d_block_cols, d_order, d_block_hints, d_plan,
-                             num_items, num_nodes, heads, head_dim, q_window_base, q_rows, d_workspace,
+    return f3s::forward_impl(d_Q, d_K, d_V, d_O, F3S_OUT_F32, d_window_offsets, d_block_cols, d_order,
+                             d_block_hints, d_plan, num_items, num_nodes, heads, head_dim, q_window_base, q_rows,
+                             d_workspace, workspace_bytes, (cudaStream_t)stream, f3s::kWaitTimeoutNs);
+}
+
+int f3s_forward_ex(const void* d_Q, const void* d_K, const void* d_V, void* d_O, int32_t o_dtype,
+                   const int32_t* d_window_offsets, const int32_t* d_block_cols, const int32_t* d_order,
+                   const uint8_t* d_block_hints, const void* d_plan, int32_t num_items, int32_t num_nodes,
+                   int32_t heads, int32_t head_dim, int32_t q_window_base, int32_t q_rows, void* d_workspace,
+                   size_t workspace_bytes, f3s_stream_t stream) {
+    return f3s::forward_impl(d_Q, d_K, d_V, d_O, o_dtype, d_window_offsets, d_block_cols, d_order, d_block_hints,
+                             d_plan, num_items, num_nodes, heads, head_dim, q_window_base, q_rows, d_workspace,
                              workspace_bytes, (cudaStream_t)stream, f3s::kWaitTimeoutNs);
 }
 

@@ -13,7 +13,7 @@ tile (32*d + 64*d bytes per head), i.e. 1.5 blocks' worth.
 """
 from __future__ import annotations
 
-from typing import List, Sequence, Tuple
+from typing import List, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -67,3 +67,119 @@ def gather_rows(slab, slabs: Sequence[Tuple[int, int]], group=None):
     bufs = [torch.empty_like(padded) for _ in sizes]
     dist.all_gather(bufs, padded, group=group)
     return torch.cat([b[:s] for b, s in zip(bufs, sizes)], dim=0)
+
+
+def sub_ranges(window_offsets, lo: int, hi: int, parts: int, window_cost: float = WINDOW_COST):
+    """[lo, hi) cut into `parts` contiguous window ranges of near-equal cost
+    (some may be empty)."""
+    off = np.asarray(window_offsets, dtype=np.int64)[lo:hi + 1]
+    local = partition_windows(off - off[0], parts, window_cost) if hi > lo else [(0, 0)] * parts
+    return [(lo + a, lo + b) for a, b in local]
+
+
+class OverlappedGather:
+    """All-gather of O rows, one sub-slab at a time, overlapped with the
+    computation of the next sub-slab.
+
+    Every rank cuts its window range into the same number of sub-slabs
+    (`sub_slabs`, cost-balanced), so every rank makes the same collective
+    calls in the same order.  After the caller has enqueued the computation
+    of sub-slab j on the current stream, `send(j, o_slab)` makes a side
+    stream wait for it, pads this rank's rows of sub-slab j to the largest
+    rank's, all-gathers them and copies every rank's rows into the full O.
+    `finish()` makes the current stream wait for the side stream and returns
+    the full O ([num_nodes, ...] on every rank).  On CPU tensors (gloo) the
+    same calls run synchronously."""
+
+    def __init__(self, window_offsets, parts, rank: int, num_nodes: int, row_shape, dtype, device,
+                 sub_slabs: int = 4, group=None):
+        import torch
+
+        self.rank, self.group, self.num_nodes = rank, group, num_nodes
+        self.parts = list(parts)
+        self.subs = [sub_ranges(window_offsets, lo, hi, sub_slabs) for lo, hi in self.parts]
+        self.rows = [[slab_rows(a, b, num_nodes) for a, b in s] for s in self.subs]
+        self.row_shape = tuple(row_shape)
+        self.device = torch.device(device)
+        self.full = torch.empty((num_nodes,) + self.row_shape, dtype=dtype, device=self.device)
+        self.cuda = self.device.type == "cuda"
+        self.stream = torch.cuda.Stream(self.device) if self.cuda else None
+        self.sub_slabs = sub_slabs
+        m = [max(r[j][1] - r[j][0] for r in self.rows) for j in range(sub_slabs)]
+        self.max_rows = m
+        self.stage = [torch.zeros((mj,) + self.row_shape, dtype=dtype, device=self.device) for mj in m]
+        self.recv = [torch.empty((len(self.parts) * mj,) + self.row_shape, dtype=dtype, device=self.device)
+                     for mj in m]
+
+    def my_sub_ranges(self):
+        return self.subs[self.rank]
+
+    def _exchange(self, j: int, o_slab):
+        import torch.distributed as dist
+
+        mj = self.max_rows[j]
+        if mj == 0:
+            return
+        r0 = slab_rows(*self.parts[self.rank], self.num_nodes)[0]
+        a, b = self.rows[self.rank][j]
+        if b > a:
+            self.stage[j][: b - a].copy_(o_slab[a - r0:b - r0])
+        views = [self.recv[j][q * mj:(q + 1) * mj] for q in range(len(self.parts))]
+        dist.all_gather(views, self.stage[j], group=self.group)
+        for q, (qa, qb) in enumerate(self.rows_of(j)):
+            if qb > qa:
+                self.full[qa:qb].copy_(views[q][: qb - qa])
+
+    def rows_of(self, j: int):
+        return [r[j] for r in self.rows]
+
+    def send(self, j: int, o_slab):
+        import torch
+
+        if not self.cuda:
+            self._exchange(j, o_slab)
+            return
+        cur = torch.cuda.current_stream(self.device)
+        self.stream.wait_stream(cur)
+        with torch.cuda.stream(self.stream):
+            self._exchange(j, o_slab)
+            o_slab.record_stream(self.stream)
+
+    def finish(self):
+        import torch
+
+        if self.cuda:
+            torch.cuda.current_stream(self.device).wait_stream(self.stream)
+        return self.full
+
+
+def sharded_forward_allgather(Q_slab, K, V, fmt, global_order, parts, rank: int, window_offsets=None,
+                              sub_slabs: int = 4, out_dtype=None, block_hints=None, plans=None, group=None,
+                              gather: Optional["OverlappedGather"] = None):
+    """This rank's windows of O computed in `sub_slabs` launches, each
+    followed by an all-gather of its rows that overlaps the next launch;
+    returns the full O on every rank (bit-identical to a 1-GPU run).
+
+    Q_slab: this rank's Q rows (slab_rows of parts[rank]); K, V replicated;
+    global_order: the balanced order of all windows; plans: optional list of
+    per-sub-slab plans (make_plan over each sub-slab's order)."""
+    import torch
+    from . import api as F
+
+    if window_offsets is None:
+        window_offsets = fmt.window_offsets.cpu().numpy()
+    dtype = out_dtype or torch.float32
+    q3 = Q_slab if Q_slab.dim() == 3 else Q_slab.unsqueeze(1)
+    og = gather or OverlappedGather(window_offsets, parts, rank, fmt.num_nodes, q3.shape[1:], dtype, Q_slab.device,
+                                    sub_slabs, group)
+    r0, _ = slab_rows(*parts[rank], fmt.num_nodes)
+    o_slab = torch.empty(q3.shape, dtype=dtype, device=Q_slab.device)
+    for j, (a, b) in enumerate(og.my_sub_ranges()):
+        ra, rb = slab_rows(a, b, fmt.num_nodes)
+        if rb > ra:
+            order_j = rank_order(global_order, a, b).contiguous()
+            F.fused3s_forward(q3[ra - r0:rb - r0], K, V, fmt, order=order_j, out=o_slab[ra - r0:rb - r0],
+                              q_window_base=a, block_hints=block_hints,
+                              plan=None if plans is None else plans[j])
+        og.send(j, o_slab)
+    return og.finish()

@@ -171,6 +171,25 @@ int f3s_forward(const void* d_Q, const void* d_K, const void* d_V, float* d_O,
                 size_t workspace_bytes, f3s_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * f3s_forward with the element type of O chosen by the caller (no reference
+ * counterpart: the reference writes fp32 O only).  Identical arguments and
+ * semantics, except d_O is [q_rows, heads, head_dim] of o_dtype: the fp32
+ * result rounded to nearest-even (F3S_OUT_F16 / F3S_OUT_BF16), which halves
+ * the O write and any later all-gather of O.  F3S_OUT_F32 is f3s_forward.
+ * ---------------------------------------------------------------------- */
+typedef enum f3s_out_dtype {
+    F3S_OUT_F32 = 0,
+    F3S_OUT_F16 = 1,
+    F3S_OUT_BF16 = 2
+} f3s_out_dtype;
+
+int f3s_forward_ex(const void* d_Q, const void* d_K, const void* d_V, void* d_O, int32_t o_dtype,
+                   const int32_t* d_window_offsets, const int32_t* d_block_cols, const int32_t* d_order,
+                   const uint8_t* d_block_hints, const void* d_plan, int32_t num_items, int32_t num_nodes,
+                   int32_t heads, int32_t head_dim, int32_t q_window_base, int32_t q_rows, void* d_workspace,
+                   size_t workspace_bytes, f3s_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Work plan for f3s_forward (no reference counterpart: the reference gives
  * each window one CTA, so one heavy window bounds the kernel's run time).
  *

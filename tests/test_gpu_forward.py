@@ -268,3 +268,24 @@ def test_forward_heavy_windows_split_heads(lib, heads, head_dim):
     assert_parity(o[rows], ref[rows], f"heavy H={heads} d={head_dim}")
     again = F.fused3s_forward(*to_gpu(q, k, v), fmt, check_status=True).cpu().numpy()
     assert np.array_equal(again, o)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16])
+def test_half_and_bf16_output_is_rounded_fp32(lib, out_dtype):
+    """fp16 / bf16 O is the fp32 O rounded to nearest-even, bit for bit (with
+    and without a plan); fp16 O also meets the parity bar."""
+    g = G.powerlaw_graph(num_nodes=2011, directed_edges=16000, max_degree=400, seed=8)
+    for heads, head_dim in ((2, 64), (4, 128)):
+        q, k, v = features_np(g.num_nodes, heads, head_dim)
+        fmt = F.convert_csr_to_block_sparse(g.num_nodes, g.row_ptr, g.col_ind)
+        Q, K, V = to_gpu(q, k, v)
+        for plan in (None, F.make_plan(fmt, heads, head_dim, max_blocks=5)):
+            o32 = F.fused3s_forward(Q, K, V, fmt, plan=plan, check_status=True)
+            o16 = F.fused3s_forward(Q, K, V, fmt, plan=plan, out_dtype=out_dtype, check_status=True)
+            assert o16.dtype == out_dtype
+            assert torch.equal(o16, o32.to(out_dtype))
+        if out_dtype == torch.float16:
+            off, cols = fmt.to_host()
+            ref = oracle.block_attention(g.num_nodes, q.astype(np.float32), k.astype(np.float32),
+                                         v.astype(np.float32), off, cols, threads=8)
+            assert_parity(o16.float().cpu().numpy(), ref, f"fp16 O H={heads} d={head_dim}")

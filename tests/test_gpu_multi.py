@@ -1,0 +1,74 @@
+"""Sharded forward with the O all-gather overlapped per sub-slab, on two GPUs
+(NCCL over NVLink): the gathered O equals the 1-GPU O bit for bit.  Skipped
+on a box with fewer than two GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                                 reason="needs two GPUs")]
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    import datetime
+    import torch.distributed as dist
+    import fused3s_b200 as F
+    from fused3s_b200 import graphs as G, shard
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        g = G.powerlaw_graph(num_nodes=6007, directed_edges=60000, max_degree=900, seed=13)
+        qf, kf, vf = (t.to(dev) for t in G.make_features(g.num_nodes, 4, 64, kind="normal", seed=7))
+        fmt = F.convert_csr_to_block_sparse(g.num_nodes, g.row_ptr, g.col_ind)
+        order = F.generate_balanced_window_order(fmt)
+        off = fmt.window_offsets.cpu().numpy()
+        parts = shard.partition_windows(off, world)
+        r0, r1 = shard.slab_rows(*parts[rank], g.num_nodes)
+        ok = []
+        for dtype in (torch.float32, torch.float16):
+            full = F.fused3s_forward(qf, kf, vf, fmt, out_dtype=dtype, check_status=True)
+            for sub in (1, 4):
+                lo, hi = parts[rank]
+                subs = shard.sub_ranges(off, lo, hi, sub)
+                plans = [F.make_plan(fmt, 4, 64, order=shard.rank_order(order, a, b).contiguous(), max_blocks=8)
+                         for a, b in subs]
+                got = shard.sharded_forward_allgather(qf[r0:r1].contiguous(), kf, vf, fmt, order, parts, rank,
+                                                      window_offsets=off, sub_slabs=sub, out_dtype=dtype,
+                                                      plans=plans)
+                torch.cuda.synchronize()
+                ok.append(bool(torch.equal(got, full)))
+        q.put((rank, all(ok)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_forward_allgather_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+    assert sorted(results) == [(0, True), (1, True)]

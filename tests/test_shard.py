@@ -85,3 +85,54 @@ def test_gather_rows_two_gloo_ranks():
     for p in procs:
         p.join(timeout=60)
     assert sorted(results) == [(0, True), (1, True)]
+
+
+def test_sub_ranges_cover_the_slab():
+    rng = np.random.default_rng(4)
+    cnt = rng.zipf(1.8, 777).clip(max=5000)
+    off = np.concatenate([[0], np.cumsum(cnt)])
+    for lo, hi in ((0, 777), (100, 101), (300, 300), (5, 640)):
+        for parts in (1, 3, 4, 8):
+            subs = shard.sub_ranges(off, lo, hi, parts)
+            assert len(subs) == parts
+            assert subs[0][0] == lo and subs[-1][1] == hi
+            for (a, b), (c, d) in zip(subs[:-1], subs[1:]):
+                assert b == c and a <= b
+
+
+def _overlap_worker(rank, world, port, result_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        n = 1501
+        rng = np.random.default_rng(2)
+        off = np.concatenate([[0], np.cumsum(rng.integers(0, 30, (n + 15) // 16))])
+        parts = shard.partition_windows(off, world)
+        full = torch.arange(n * 6, dtype=torch.float32).reshape(n, 2, 3)
+        ok = True
+        for sub_slabs in (1, 3, 4):
+            og = shard.OverlappedGather(off, parts, rank, n, (2, 3), torch.float32, "cpu", sub_slabs)
+            r0, r1 = shard.slab_rows(*parts[rank], n)
+            o_slab = torch.full((r1 - r0, 2, 3), -1.0)
+            for j, (a, b) in enumerate(og.my_sub_ranges()):
+                ra, rb = shard.slab_rows(a, b, n)
+                o_slab[ra - r0:rb - r0] = full[ra:rb]  # the "computation" of sub-slab j
+                og.send(j, o_slab)
+            ok = ok and bool(torch.equal(og.finish(), full))
+        result_q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_overlapped_gather_two_gloo_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_overlap_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert sorted(results) == [(0, True), (1, True)]
