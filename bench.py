@@ -468,8 +468,8 @@ def run_ours(args):
         subs = shard.sub_ranges(off_h, lo, hi, args.sub_slabs)
         sub_plans = None
         if plan is not None:
-            sub_plans = [F.make_plan(fmt, H, d, order=shard.rank_order(order, a, b).contiguous(), max_blocks=T)
-                         for a, b in subs]
+            # piece size from each sub-slab's own blocks (a quarter of an SM's share)
+            sub_plans = [F.make_plan(fmt, H, d, order=shard.rank_order(order, a, b).contiguous()) for a, b in subs]
         og = shard.OverlappedGather(off_h, parts, rank, N, (H, d), O.dtype, dev, args.sub_slabs)
 
         def fwd_gather():

@@ -245,14 +245,19 @@ def auto_piece_blocks(num_blocks: int, device=None) -> int:
 def make_plan(fmt: BlockSparseFormat, heads: int, head_dim: int, order: Optional[torch.Tensor] = None,
               max_blocks: Optional[int] = None) -> ForwardPlan:
     """Plan for fused3s_forward over the windows in `order` (default: the
-    balanced order of all windows)."""
+    balanced order of all windows).  max_blocks: piece size (default
+    auto_piece_blocks of the listed windows' blocks)."""
     lib = _lib.load()
     device = fmt.window_offsets.device
     if order is None:
         order = generate_balanced_window_order(fmt)
+        nb = max(fmt.num_blocks, 1)
+    else:
+        order = order.to(device=device, dtype=torch.int32).contiguous()
+        off = fmt.window_offsets
+        nb = max(int((off[order.long() + 1] - off[order.long()]).sum().item()) if order.numel() else 0, 1)
     order = order.to(device=device, dtype=torch.int32).contiguous()
     n = int(order.numel())
-    nb = max(fmt.num_blocks, 1)
     if max_blocks is None:
         max_blocks = auto_piece_blocks(nb, device)
     size = lib.f3s_plan_size(n, nb, int(max_blocks), heads, head_dim)

@@ -44,8 +44,11 @@ def _worker(rank, world, port, q):
         parts = shard.partition_windows(off, world)
         r0, r1 = shard.slab_rows(*parts[rank], g.num_nodes)
         ok = []
+        # pieces are cut per window (at most 8 blocks), so the planned 1-GPU
+        # run and every planned slab agree bit for bit
+        full_plan = F.make_plan(fmt, 4, 64, max_blocks=8)
         for dtype in (torch.float32, torch.float16):
-            full = F.fused3s_forward(qf, kf, vf, fmt, out_dtype=dtype, check_status=True)
+            full = F.fused3s_forward(qf, kf, vf, fmt, out_dtype=dtype, plan=full_plan, check_status=True)
             for sub in (1, 4):
                 lo, hi = parts[rank]
                 subs = shard.sub_ranges(off, lo, hi, sub)
