@@ -453,6 +453,7 @@ def run_ours(args):
     # launch (shard.sharded_forward_allgather)
     gather_ms = None
     overlap_ms = None
+    peer_ms = None
     if world > 1 and args.gather:
         slabs = [shard.slab_rows(a, b, N) for a, b in parts]
         ge = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
@@ -489,6 +490,23 @@ def run_ours(args):
         t = torch.tensor([ge[2].elapsed_time(ge[3]) / args.steps], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         overlap_ms = float(t.item())
+        del og
+        # (3) the same with the rows moved by the copy engines into IPC-mapped
+        # peer buffers (no SMs taken from the fused kernel)
+        og = shard.PeerGather(off_h, parts, rank, N, (H, d), O.dtype, dev, args.sub_slabs)
+        for _ in range(2):
+            fwd_gather()
+        dist.barrier()
+        torch.cuda.synchronize()
+        ge[2].record(stream)
+        for _ in range(args.steps):
+            fwd_gather()
+        ge[3].record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([ge[2].elapsed_time(ge[3]) / args.steps], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        peer_ms = float(t.item())
+        og.close()
         del og
 
     # roofline of the fused kernel (per launch, this rank's share)
@@ -540,6 +558,7 @@ def run_ours(args):
             result["allgather_o_ms"] = gather_ms
             result["forward_then_allgather_ms"] = ms_per_step + gather_ms
             result["forward_allgather_overlapped_ms"] = overlap_ms
+            result["forward_peer_copy_overlapped_ms"] = peer_ms
             result["sub_slabs"] = args.sub_slabs
         emit(result)
     if world > 1:

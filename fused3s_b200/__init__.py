@@ -19,9 +19,12 @@ from .api import (
     fused3s_forward,
     generate_balanced_window_order,
     load_csr_graph,
+    load_csr_graph_device,
     make_plan,
+    parse_int32_text,
     workspace_status,
 )
+from . import torch_op  # registers torch.ops.fused3s.block_attention
 
 __all__ = [
     "BlockSparseFormat",
@@ -38,5 +41,7 @@ __all__ = [
     "fused3s_forward",
     "generate_balanced_window_order",
     "load_csr_graph",
+    "load_csr_graph_device",
+    "parse_int32_text",
     "workspace_status",
 ]

@@ -22,6 +22,8 @@ F3S_ERR_TIMEOUT = 6
 F3S_ERR_BAD_FORMAT = 7
 F3S_ERR_TOO_LARGE = 8
 
+F3S_IPC_HANDLE_BYTES = 64
+
 F3S_OUT_F32 = 0
 F3S_OUT_F16 = 1
 F3S_OUT_BF16 = 2
@@ -48,6 +50,13 @@ SIGNATURES = {
                                    _SZ, _P]),
     "f3s_forward_ex": (ctypes.c_int, [_P, _P, _P, _P, _I32, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
                                       _P, _SZ, _P]),
+    "f3s_parse_int32_workspace_size": (_SZ, [_I64]),
+    "f3s_parse_int32": (ctypes.c_int, [_P, _I64, _P, _I64, ctypes.POINTER(ctypes.c_int64), _P, _SZ, _P]),
+    "f3s_peer_alloc": (ctypes.c_int, [_SZ, ctypes.POINTER(ctypes.c_void_p), _P]),
+    "f3s_peer_open": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    "f3s_peer_close": (ctypes.c_int, [_P]),
+    "f3s_peer_free": (ctypes.c_int, [_P]),
+    "f3s_peer_copy": (ctypes.c_int, [_P, _P, _SZ, _P]),
     "f3s_plan_size": (_SZ, [_I32, _I64, _I32, _I32, _I32]),
     "f3s_make_plan": (ctypes.c_int, [_P, _P, _I32, _I64, _I32, _I32, _I32, _P, _SZ, _P]),
     "f3s_block_hints_workspace_size": (_SZ, [_I32]),

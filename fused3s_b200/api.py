@@ -43,8 +43,8 @@ class GraphData:
     """CSR graph (include/utils.cuh:19-24)."""
     num_nodes: int
     num_edges: int
-    row_ptr: np.ndarray  # int32 [num_nodes + 1]
-    col_ind: np.ndarray  # int32 [num_edges]
+    row_ptr: "np.ndarray | torch.Tensor"  # int32 [num_nodes + 1] (host, or device from load_csr_graph_device)
+    col_ind: "np.ndarray | torch.Tensor"  # int32 [num_edges]
 
 
 @dataclasses.dataclass
@@ -137,6 +137,68 @@ def _default_device(device) -> torch.device:
 # ----------------------------------------------------------------------------
 # converter / order
 # ----------------------------------------------------------------------------
+
+_TEXT_CHUNK = (1 << 31) - 2  # f3s_parse_int32 takes fewer bytes per call
+
+
+def parse_int32_text(text, max_count: Optional[int] = None, device=None) -> torch.Tensor:
+    """Whitespace-separated decimal integers decoded on the GPU
+    (f3s_parse_int32).  `text`: bytes, a numpy uint8 array or a uint8 tensor
+    (host or device).  Returns int32 values on `device`.  Texts longer than
+    one call takes are cut at a separator and decoded piece by piece."""
+    lib = _lib.load()
+    device = _default_device(device)
+    if isinstance(text, (bytes, bytearray, memoryview)):
+        text = np.frombuffer(bytes(text), dtype=np.uint8)
+    if isinstance(text, np.ndarray):
+        host = text.view(np.uint8).reshape(-1)
+        dev_text = torch.from_numpy(host).to(device)
+    else:
+        dev_text = text.to(device=device, dtype=torch.uint8).contiguous().view(-1)
+        host = None
+    n = int(dev_text.numel())
+    cap = (n + 1) // 2 if max_count is None else int(max_count)
+    out = torch.empty(max(cap, 1), dtype=torch.int32, device=device)
+    got = 0
+    start = 0
+    while start < n:
+        end = min(n, start + _TEXT_CHUNK)
+        if end < n:  # cut after the last separator of this piece
+            piece = host[start:end] if host is not None else dev_text[start:end].cpu().numpy()
+            seps = np.flatnonzero(np.isin(piece, np.frombuffer(b" \t\r\n", dtype=np.uint8)))
+            if seps.size == 0:
+                raise ValueError("text has a token longer than one parse call")
+            end = start + int(seps[-1]) + 1
+        nb = end - start
+        ws = _WS.get(device, "text", lib.f3s_parse_int32_workspace_size(nb))
+        cnt = _lib.ctypes.c_int64(0)
+        with torch.cuda.device(device):
+            st = lib.f3s_parse_int32(dev_text.data_ptr() + start, nb, out.data_ptr() + 4 * got, cap - got, cnt,
+                                     _ptr(ws), ws.numel(), _stream_ptr(device))
+        check(st, "f3s_parse_int32")
+        got += cnt.value
+        start = end
+    return out[:got]
+
+
+def load_csr_graph_device(dataset_dir: str, device=None) -> GraphData:
+    """load_csr_graph with the text decoded on the GPU: the files' bytes go to
+    the device as they are (include/utils.cuh:26-40, column file col_idx.txt
+    or col_ind.txt).  Returns GraphData whose row_ptr / col_ind are int32
+    device tensors, ready for convert_csr_to_block_sparse."""
+    device = _default_device(device)
+    with open(os.path.join(dataset_dir, "meta.txt")) as f:
+        num_nodes, num_edges = (int(x) for x in f.read().split()[:2])
+    col_path = os.path.join(dataset_dir, "col_idx.txt")
+    if not os.path.exists(col_path):
+        col_path = os.path.join(dataset_dir, "col_ind.txt")
+    row_ptr = parse_int32_text(np.fromfile(os.path.join(dataset_dir, "row_ptr.txt"), dtype=np.uint8),
+                               num_nodes + 1, device)
+    col_ind = parse_int32_text(np.fromfile(col_path, dtype=np.uint8), num_edges, device)
+    if row_ptr.numel() != num_nodes + 1 or col_ind.numel() != num_edges:
+        raise ValueError(f"{dataset_dir}: sizes disagree with meta.txt")
+    return GraphData(num_nodes, num_edges, row_ptr, col_ind)
+
 
 def convert_csr_to_block_sparse(num_nodes: int, row_ptr, col_ind, device=None) -> BlockSparseFormat:
     """CSR -> block-sparse row windows on the GPU (src/converter.cu:13-44).

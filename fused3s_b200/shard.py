@@ -114,6 +114,15 @@ class OverlappedGather:
     def my_sub_ranges(self):
         return self.subs[self.rank]
 
+    def start(self):
+        """Called before the first sub-slab of a step (nothing to do here)."""
+
+    def output_slab(self, shape, dtype):
+        """Where the forward writes this rank's O rows."""
+        import torch
+
+        return torch.empty(shape, dtype=dtype, device=self.device)
+
     def _exchange(self, j: int, o_slab):
         import torch.distributed as dist
 
@@ -173,7 +182,8 @@ def sharded_forward_allgather(Q_slab, K, V, fmt, global_order, parts, rank: int,
     og = gather or OverlappedGather(window_offsets, parts, rank, fmt.num_nodes, q3.shape[1:], dtype, Q_slab.device,
                                     sub_slabs, group)
     r0, _ = slab_rows(*parts[rank], fmt.num_nodes)
-    o_slab = torch.empty(q3.shape, dtype=dtype, device=Q_slab.device)
+    o_slab = og.output_slab(q3.shape, dtype)
+    og.start()
     for j, (a, b) in enumerate(og.my_sub_ranges()):
         ra, rb = slab_rows(a, b, fmt.num_nodes)
         if rb > ra:
@@ -183,3 +193,136 @@ def sharded_forward_allgather(Q_slab, K, V, fmt, global_order, parts, rank: int,
                               plan=None if plans is None else plans[j])
         og.send(j, o_slab)
     return og.finish()
+
+
+class _DeviceBuffer:
+    """A raw device allocation seen by torch (zero-copy) as uint8[nbytes]."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerGather:
+    """All-gather of O rows by the copy engines over NVLink, overlapped with
+    the fused kernel.
+
+    Every rank allocates its full O in an IPC-exportable buffer
+    (f3s_peer_alloc) and maps every other rank's (f3s_peer_open); the forward
+    writes this rank's rows in place (`output_slab`).  After the
+    computation of sub-slab j is enqueued, `send(j, o_slab)` makes a side
+    stream wait for it and copies this rank's rows of sub-slab j into every
+    other rank's full O (f3s_peer_copy: cudaMemcpyAsync, a copy engine, no SMs --
+    so it runs beside a kernel that holds every SM, where a collective kernel
+    would wait for one).  Two stream-ordered handshakes (a one-element NCCL
+    all-reduce on the side stream) bracket a step: `start()` keeps peers from
+    writing into this rank's full O before its earlier work on it is done,
+    and `finish()` tells every rank that all copies into its buffer are
+    complete, then makes the current stream wait.  Same interface as
+    OverlappedGather; `close()` unmaps and frees (collective)."""
+
+    def __init__(self, window_offsets, parts, rank: int, num_nodes: int, row_shape, dtype, device,
+                 sub_slabs: int = 4, group=None):
+        import ctypes
+        import torch
+        import torch.distributed as dist
+        from . import _lib
+
+        self.lib = _lib.load()
+        self.rank, self.group, self.num_nodes = rank, group, num_nodes
+        self.parts = list(parts)
+        self.subs = [sub_ranges(window_offsets, lo, hi, sub_slabs) for lo, hi in self.parts]
+        self.rows = [[slab_rows(a, b, num_nodes) for a, b in s] for s in self.subs]
+        self.device = torch.device(device)
+        self.row_shape = tuple(row_shape)
+        elem = torch.empty(0, dtype=dtype).element_size()
+        self.row_bytes = int(np.prod(self.row_shape)) * elem
+        nbytes = max(num_nodes * self.row_bytes, 1)
+        with torch.cuda.device(self.device):
+            ptr = ctypes.c_void_p()
+            handle = ctypes.create_string_buffer(_lib.F3S_IPC_HANDLE_BYTES)
+            _lib.check(self.lib.f3s_peer_alloc(nbytes, ctypes.byref(ptr), handle), "f3s_peer_alloc")
+            self.ptr = ptr.value
+            handles = [None] * len(self.parts)
+            dist.all_gather_object(handles, handle.raw, group=group)
+            self.peer_ptrs = []
+            for q, h in enumerate(handles):
+                if q == rank:
+                    self.peer_ptrs.append(self.ptr)
+                    continue
+                p = ctypes.c_void_p()
+                _lib.check(self.lib.f3s_peer_open(ctypes.create_string_buffer(h, len(h)), ctypes.byref(p)),
+                           "f3s_peer_open")
+                self.peer_ptrs.append(p.value)
+            raw = torch.as_tensor(_DeviceBuffer(self.ptr, nbytes), device=self.device)
+            self.full = raw[: num_nodes * self.row_bytes].view(dtype).view((num_nodes,) + self.row_shape)
+            self.stream = torch.cuda.Stream(self.device)
+            self.flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def my_sub_ranges(self):
+        return self.subs[self.rank]
+
+    def output_slab(self, shape, dtype):
+        """This rank's rows of the full O: the forward writes them in place."""
+        r0, r1 = slab_rows(*self.parts[self.rank], self.num_nodes)
+        if self.full.dtype != dtype or tuple(shape) != (r1 - r0,) + self.row_shape:
+            raise ValueError("output slab shape / dtype disagree with the gather buffer")
+        return self.full[r0:r1]
+
+    def _handshake(self):
+        import torch.distributed as dist
+
+        dist.all_reduce(self.flag, group=self.group)
+
+    def start(self):
+        import torch
+
+        self.stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self.stream):
+            self._handshake()
+
+    def send(self, j: int, o_slab):
+        import torch
+
+        self.stream.wait_stream(torch.cuda.current_stream(self.device))
+        r0 = slab_rows(*self.parts[self.rank], self.num_nodes)[0]
+        a, b = self.rows[self.rank][j]
+        if b > a:
+            src = o_slab.data_ptr() + (a - r0) * self.row_bytes
+            sptr = self.stream.cuda_stream
+            for q, dst in enumerate(self.peer_ptrs):
+                if dst + a * self.row_bytes == src:
+                    continue  # written in place by the forward
+                _lib_check(self.lib.f3s_peer_copy(dst + a * self.row_bytes, src, (b - a) * self.row_bytes, sptr))
+        o_slab.record_stream(self.stream)
+
+    def finish(self):
+        import torch
+
+        with torch.cuda.stream(self.stream):
+            self._handshake()
+        torch.cuda.current_stream(self.device).wait_stream(self.stream)
+        return self.full
+
+    def close(self):
+        """Collective: every rank unmaps the others' buffers, then frees its own."""
+        import torch
+        import torch.distributed as dist
+
+        if self.ptr is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for q, p in enumerate(self.peer_ptrs):
+            if q != self.rank:
+                self.lib.f3s_peer_close(p)
+        dist.barrier(group=self.group)
+        self.full = None
+        self.lib.f3s_peer_free(self.ptr)
+        self.ptr = None
+
+
+def _lib_check(status: int):
+    from . import _lib
+
+    _lib.check(status, "f3s_peer_copy")

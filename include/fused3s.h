@@ -256,6 +256,44 @@ int f3s_half_from_float(const float* d_in, void* d_out, int64_t n, f3s_stream_t 
 int f3s_selftest_wait_timeout(uint64_t timeout_ns, void* d_workspace, size_t workspace_bytes,
                               f3s_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Decimal text -> int32 on the GPU (the reference reads row_ptr.txt and
+ * col_idx.txt with std::ifstream >>, include/utils.cuh:26-40; here the file
+ * bytes are copied to the device as they are and decoded there).
+ *
+ * d_text: n_bytes of whitespace-separated integers (space, tab, CR, LF;
+ * optional sign).  Writes the numbers in order to d_out[0 .. *h_count) and
+ * synchronises the stream.  Errors: F3S_ERR_INVALID_VALUE for any other
+ * byte or a malformed number, F3S_ERR_TOO_LARGE for a value outside int32 or
+ * n_bytes >= 2^31 - 1 (split larger files at a separator), F3S_ERR_WORKSPACE
+ * when the text holds more than max_count numbers.
+ * ---------------------------------------------------------------------- */
+size_t f3s_parse_int32_workspace_size(int64_t n_bytes);
+int f3s_parse_int32(const char* d_text, int64_t n_bytes, int32_t* d_out, int64_t max_count, int64_t* h_count,
+                    void* d_workspace, size_t workspace_bytes, f3s_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Peer buffers for exchanging O between the ranks of a sharded forward (no
+ * reference counterpart: the reference runs on one GPU).
+ *
+ * f3s_peer_alloc allocates `bytes` of device memory on the current device
+ * and writes its CUDA IPC handle (F3S_IPC_HANDLE_BYTES bytes) to
+ * ipc_handle; another process on the box passes the handle to
+ * f3s_peer_open to map the buffer (peer access enabled over NVLink), and
+ * unmaps it with f3s_peer_close before the owner calls f3s_peer_free.
+ * f3s_peer_copy is a stream-ordered copy between any two device pointers
+ * (local or mapped): it runs on a copy engine, so it overlaps kernels that
+ * hold every SM.  Copies into another rank's buffer are complete when the
+ * copying stream passes them; a stream-ordered collective after them tells
+ * the owner.
+ * ---------------------------------------------------------------------- */
+#define F3S_IPC_HANDLE_BYTES 64
+int f3s_peer_alloc(size_t bytes, void** d_ptr, void* ipc_handle);
+int f3s_peer_open(const void* ipc_handle, void** d_ptr);
+int f3s_peer_close(void* d_ptr);
+int f3s_peer_free(void* d_ptr);
+int f3s_peer_copy(void* d_dst, const void* d_src, size_t bytes, f3s_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

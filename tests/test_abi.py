@@ -53,6 +53,13 @@ def test_invalid_arguments_are_rejected_without_touching_the_gpu(lib):
     assert lib.f3s_convert(None, None, -1, 0, None, None, None, 0, None, None) == _lib.F3S_ERR_INVALID_VALUE
     assert lib.f3s_window_order(None, -3, None, None, 0, None) == _lib.F3S_ERR_INVALID_VALUE
     assert lib.f3s_half_from_float(None, None, -1, None) == _lib.F3S_ERR_INVALID_VALUE
+    n = _lib.ctypes.c_int64(0)
+    assert lib.f3s_parse_int32(None, -1, None, 0, n, 256, 256, None) == _lib.F3S_ERR_INVALID_VALUE
+    assert lib.f3s_parse_int32(None, 1 << 33, None, 0, n, 256, 256, None) == _lib.F3S_ERR_TOO_LARGE
+    assert lib.f3s_parse_int32(None, 0, None, 0, n, 256, 256, None) == 0 and n.value == 0
+    assert lib.f3s_peer_copy(None, None, 16, None) == _lib.F3S_ERR_INVALID_VALUE
+    assert lib.f3s_forward_ex(None, None, None, None, 7, None, None, None, None, None, 1, 10, 1, 64, 0, 10, 256,
+                              256, None) == _lib.F3S_ERR_INVALID_VALUE
 
 
 def test_product_package_does_not_reference_the_oracle():

@@ -59,6 +59,15 @@ def _worker(rank, world, port, q):
                                                       plans=plans)
                 torch.cuda.synchronize()
                 ok.append(bool(torch.equal(got, full)))
+                # the same through the copy engines (IPC-mapped peer buffers), two steps
+                pg = shard.PeerGather(off, parts, rank, g.num_nodes, (4, 64), dtype, dev, sub)
+                for _ in range(2):
+                    got = shard.sharded_forward_allgather(qf[r0:r1].contiguous(), kf, vf, fmt, order, parts, rank,
+                                                          window_offsets=off, sub_slabs=sub, out_dtype=dtype,
+                                                          plans=plans, gather=pg)
+                    torch.cuda.synchronize()
+                    ok.append(bool(torch.equal(got, full)))
+                pg.close()
         q.put((rank, all(ok)))
     finally:
         dist.destroy_process_group()
