@@ -139,13 +139,32 @@ def _default_device(device) -> torch.device:
 # ----------------------------------------------------------------------------
 
 _TEXT_CHUNK = (1 << 31) - 2  # f3s_parse_int32 takes fewer bytes per call
+_TEXT_SEPARATORS = np.frombuffer(b" \t\r\n", dtype=np.uint8)
+
+
+def text_pieces(host_text: np.ndarray, limit: int = _TEXT_CHUNK):
+    """[start, end) byte ranges of at most `limit` bytes that cover the text
+    and end just after a separator (except the last), so no number is cut."""
+    n = int(host_text.shape[0])
+    cuts, start = [], 0
+    while start < n:
+        end = min(n, start + limit)
+        if end < n:
+            seps = np.flatnonzero(np.isin(host_text[start:end], _TEXT_SEPARATORS))
+            if seps.size == 0:
+                raise ValueError("text has a token longer than one parse call")
+            end = start + int(seps[-1]) + 1
+        cuts.append((start, end))
+        start = end
+    return cuts
 
 
 def parse_int32_text(text, max_count: Optional[int] = None, device=None) -> torch.Tensor:
     """Whitespace-separated decimal integers decoded on the GPU
     (f3s_parse_int32).  `text`: bytes, a numpy uint8 array or a uint8 tensor
     (host or device).  Returns int32 values on `device`.  Texts longer than
-    one call takes are cut at a separator and decoded piece by piece."""
+    one call takes are cut at a separator (text_pieces) and decoded piece by
+    piece."""
     lib = _lib.load()
     device = _default_device(device)
     if isinstance(text, (bytes, bytearray, memoryview)):
@@ -157,18 +176,13 @@ def parse_int32_text(text, max_count: Optional[int] = None, device=None) -> torc
         dev_text = text.to(device=device, dtype=torch.uint8).contiguous().view(-1)
         host = None
     n = int(dev_text.numel())
+    if n > _TEXT_CHUNK and host is None:
+        host = dev_text.cpu().numpy()
+    pieces = text_pieces(host) if host is not None else [(0, n)] if n else []
     cap = (n + 1) // 2 if max_count is None else int(max_count)
     out = torch.empty(max(cap, 1), dtype=torch.int32, device=device)
     got = 0
-    start = 0
-    while start < n:
-        end = min(n, start + _TEXT_CHUNK)
-        if end < n:  # cut after the last separator of this piece
-            piece = host[start:end] if host is not None else dev_text[start:end].cpu().numpy()
-            seps = np.flatnonzero(np.isin(piece, np.frombuffer(b" \t\r\n", dtype=np.uint8)))
-            if seps.size == 0:
-                raise ValueError("text has a token longer than one parse call")
-            end = start + int(seps[-1]) + 1
+    for start, end in pieces:
         nb = end - start
         ws = _WS.get(device, "text", lib.f3s_parse_int32_workspace_size(nb))
         cnt = _lib.ctypes.c_int64(0)
@@ -177,7 +191,6 @@ def parse_int32_text(text, max_count: Optional[int] = None, device=None) -> torc
                                      _ptr(ws), ws.numel(), _stream_ptr(device))
         check(st, "f3s_parse_int32")
         got += cnt.value
-        start = end
     return out[:got]
 
 

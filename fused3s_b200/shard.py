@@ -294,7 +294,7 @@ class PeerGather:
                 if dst + a * self.row_bytes == src:
                     continue  # written in place by the forward
                 _lib_check(self.lib.f3s_peer_copy(dst + a * self.row_bytes, src, (b - a) * self.row_bytes, sptr))
-        o_slab.record_stream(self.stream)
+        # o_slab is this gatherer's own buffer (output_slab), alive as long as it is
 
     def finish(self):
         import torch

@@ -3,6 +3,7 @@ what include/fused3s.h declares.  No compute call is made here."""
 import ctypes
 import re
 
+import numpy as np
 import pytest
 
 from conftest import ROOT
@@ -68,3 +69,21 @@ def test_product_package_does_not_reference_the_oracle():
     for path in list(pkg.glob("*.py")) + list((pkg / "csrc").glob("*")):
         text = path.read_text()
         assert "import oracle" not in text and "liboracle" not in text and "libf3s_ref" not in text, path
+
+
+def test_text_pieces_cut_at_separators():
+    """Host side of the GPU text reader: pieces of at most `limit` bytes that
+    end after a separator cover the text, and no number is split."""
+    from fused3s_b200.api import text_pieces
+    rng = np.random.default_rng(0)
+    vals = rng.integers(0, 10**9, 5000)
+    text = np.frombuffer(("\n".join(str(v) for v in vals) + "\n").encode(), dtype=np.uint8)
+    for limit in (16, 64, 1000, len(text), len(text) + 5):
+        cuts = text_pieces(text, limit)
+        assert cuts[0][0] == 0 and cuts[-1][1] == len(text)
+        assert all(b - a <= limit for a, b in cuts)
+        assert all(b == c for (_, b), (c, _) in zip(cuts[:-1], cuts[1:]))
+        joined = [int(x) for a, b in cuts for x in bytes(text[a:b]).split()]
+        assert np.array_equal(joined, vals)
+    with pytest.raises(ValueError):
+        text_pieces(np.frombuffer(b"123456789 1", dtype=np.uint8), 4)
