@@ -535,13 +535,14 @@ def run_ours(args):
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f16 in / f32 accumulate", "data": "synthetic",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": args.config, "description": cfg.description, "num_nodes": N, "num_edges": E,
                        "heads": H, "head_dim": d, "blocks": B, "row_windows": nrw,
                        "parallelism": f"row-window shards x{world}, K/V replicated",
                        "l2": "inputs larger than L2" if (Kf.numel() + Vf.numel()) * 2 > 126e6 else
                              "inputs fit in L2 (no flush)",
                        "convert_ms": convert_ms, "order_ms": order_ms, "l2_hints": args.l2_hints, "cuda_graph": args.graph, "o_dtype": args.out_dtype,
+                       "precision": "f16 Q/K/V and P on the tensor cores, f32 accumulation and softmax state",
                        "hints_ms": hints_ms, "split": args.split,
                        "piece_blocks": plan.max_blocks if plan is not None else None, "plan_ms": plan_ms},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
