@@ -201,4 +201,46 @@ inline void forward(const void* Q, const void* K, const void* V, float* O, const
           "f3s_forward");
 }
 
+// Work plan (f3s_make_plan) owned by the caller: windows above
+// max_blocks_per_piece blocks run as several pieces, merged in piece order.
+// Build once per graph, window set and (heads, head_dim).
+struct Plan {
+    DeviceBuffer<unsigned char> buf;
+    Plan(const int* window_offsets, const int* order, int num_items, int64_t num_blocks, int max_blocks_per_piece,
+         int heads, int head_dim, cudaStream_t stream = 0)
+        : buf(f3s_plan_size(num_items, num_blocks, max_blocks_per_piece, heads, head_dim)) {
+        if (buf.count == 0) throw Error(F3S_ERR_INVALID_VALUE, "f3s_plan_size");
+        check(f3s_make_plan(window_offsets, order, num_items, num_blocks, max_blocks_per_piece, heads, head_dim,
+                            buf.ptr, buf.count, reinterpret_cast<f3s_stream_t>(stream)),
+              "f3s_make_plan");
+    }
+    const void* get() const { return buf.ptr; }
+};
+
+// Per-block L2 eviction hints (f3s_block_hints) for the windows in `order`,
+// with half of `l2_bytes` as the keep budget; d_hints holds num_blocks bytes.
+inline void block_hints(const int* window_offsets, const int* block_cols, const int* order, int num_items,
+                        int num_row_windows, int heads, int head_dim, int64_t l2_bytes, unsigned char* d_hints,
+                        cudaStream_t stream = 0) {
+    DeviceBuffer<unsigned char> ws(f3s_block_hints_workspace_size(num_row_windows));
+    check(f3s_block_hints(window_offsets, block_cols, order, num_items, num_row_windows,
+                          16LL * heads * head_dim * 2 * 2, l2_bytes / 2, d_hints, ws.ptr, ws.count,
+                          reinterpret_cast<f3s_stream_t>(stream)),
+          "f3s_block_hints");
+    check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize");  // ws is freed on return
+}
+
+// The extended forward with an optional plan and hints and O in
+// F3S_OUT_F32 / F3S_OUT_F16 / F3S_OUT_BF16 (the fp32 result rounded to
+// nearest); d_O is [num_nodes, heads, head_dim] of that type.
+inline void forward_ex(const void* Q, const void* K, const void* V, void* O, int o_dtype, const int* window_offsets,
+                       const int* block_cols, const int* order, const unsigned char* block_hints, const Plan* plan,
+                       int num_items, int num_nodes, int heads, int head_dim, void* workspace,
+                       size_t workspace_bytes, cudaStream_t stream = 0) {
+    check(f3s_forward_ex(Q, K, V, O, o_dtype, window_offsets, block_cols, order, block_hints,
+                         plan ? plan->get() : nullptr, num_items, num_nodes, heads, head_dim, 0, num_nodes, workspace,
+                         workspace_bytes, reinterpret_cast<f3s_stream_t>(stream)),
+          "f3s_forward_ex");
+}
+
 }  // namespace fused3s

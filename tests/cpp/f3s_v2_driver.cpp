@@ -111,7 +111,25 @@ int main(int argc, char** argv) {
         }
         const double rel = den > 0 ? std::sqrt(num / den) : std::sqrt(num);
         std::printf("extended forward: maxabs=%.3e relL2=%.3e\n", maxabs, rel);
-        const bool ok = mismatches == 0 && maxabs <= 2e-2 && rel <= 1e-3;
+
+        // 3. work plan (heavy windows in pieces of at most 4 blocks) and fp16 O
+        const int64_t nblocks = (int64_t)format.block_col_indices.size();
+        fused3s::Plan plan(dOff.ptr, dOrder.ptr, nrw, std::max<int64_t>(nblocks, 1), 4, 1, feat_dim);
+        fused3s::DeviceBuffer<unsigned short> dO16(feat_size);
+        fused3s::forward_ex(dQ.ptr, dK.ptr, dV.ptr, dO16.ptr, F3S_OUT_F16, dOff.ptr, dCols.ptr, dOrder.ptr, nullptr,
+                            &plan, nrw, graph.num_nodes, 1, feat_dim, dWs.ptr, wsz);
+        fused3s::check(f3s_workspace_status(dWs.ptr, nullptr), "f3s_forward_ex (device)");
+        std::vector<__half> h_O16(feat_size);
+        CUDA_OK(cudaMemcpy(h_O16.data(), dO16.ptr, feat_size * 2, cudaMemcpyDeviceToHost));
+        double num16 = 0, maxabs16 = 0;
+        for (size_t i = 0; i < (size_t)graph.num_nodes * feat_dim; ++i) {
+            const double e = (double)__half2float(h_O16[i]) - h_O_cpu16[i];
+            num16 += e * e;
+            maxabs16 = std::max(maxabs16, std::fabs(e));
+        }
+        const double rel16 = den > 0 ? std::sqrt(num16 / den) : std::sqrt(num16);
+        std::printf("planned fp16 forward: maxabs=%.3e relL2=%.3e\n", maxabs16, rel16);
+        const bool ok = mismatches == 0 && maxabs <= 2e-2 && rel <= 1e-3 && maxabs16 <= 2e-2 && rel16 <= 1e-3;
         std::printf("%s\n", ok ? "SUCCESS" : "FAILURE");
         return ok ? 0 : 1;
     } catch (const std::exception& e) {
