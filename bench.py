@@ -335,12 +335,23 @@ def run_ours(args):
     # work plan: heavy windows cut into pieces (computed once per graph and rank)
     plan = None
     plan_ms = None
+    chunk_cols = None
     if args.split != "off":
         my_blocks_total = int((fmt.window_offsets[1:] - fmt.window_offsets[:-1])[lo:hi].sum().item())
-        T = F.auto_piece_blocks(my_blocks_total, dev) if args.split == "auto" else int(args.split)
+        chunked = args.split.startswith("chunked")
+        if args.split == "auto" or chunked:
+            T = F.auto_piece_blocks(my_blocks_total, dev)
+        else:
+            T = int(args.split)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        plan = F.make_plan(fmt, H, d, order=my_order, max_blocks=T)
+        if chunked:
+            # column-chunked plan: all SMs sweep one L2-sized range of block
+            # columns at a time ("chunked" or "chunked:<block columns>")
+            chunk_cols = int(args.split.split(":")[1]) if ":" in args.split else None
+            plan = F.make_chunked_plan(fmt, H, d, order=my_order, chunk_cols=chunk_cols, max_blocks=T)
+        else:
+            plan = F.make_plan(fmt, H, d, order=my_order, max_blocks=T)
         torch.cuda.synchronize()
         plan_ms = (time.perf_counter() - t0) * 1e3
     plan_ptr = plan.buffer.data_ptr() if plan is not None else None
@@ -582,7 +593,8 @@ def main(argv=None):
     ap.add_argument("--graph", default="on", choices=["on", "off"],
                     help="replay the timed step as a CUDA graph")
     ap.add_argument("--split", default="auto",
-                    help="cut windows above this many blocks into pieces: auto, off or a number")
+                    help="cut windows above this many blocks into pieces: auto, off, a number, or "
+                         "chunked[:block columns] (pieces cut at column-chunk boundaries, swept chunk by chunk)")
     ap.add_argument("--l2-hints", default="on", choices=["on", "off"],
                     help="per block L2 eviction hints (computed once per graph)")
     ap.add_argument("--no-e2e", action="store_true")

@@ -20,6 +20,8 @@ from .api import (
     generate_balanced_window_order,
     load_csr_graph,
     load_csr_graph_device,
+    column_chunk_pieces,
+    make_chunked_plan,
     make_plan,
     parse_int32_text,
     workspace_status,
@@ -36,6 +38,8 @@ __all__ = [
     "convert_csr_to_block_sparse",
     "f3s_1tb1rw_kernel",
     "make_plan",
+    "make_chunked_plan",
+    "column_chunk_pieces",
     "float2half",
     "forward_workspace",
     "fused3s_forward",

@@ -346,6 +346,97 @@ def make_plan(fmt: BlockSparseFormat, heads: int, head_dim: int, order: Optional
     return ForwardPlan(buf, heads, head_dim, int(max_blocks))
 
 
+def column_chunk_pieces(window_offsets: np.ndarray, block_cols: np.ndarray, order: np.ndarray, chunk_cols: int,
+                        max_blocks: int = 0):
+    """Pieces of a column-chunked plan, built on the host.
+
+    Every listed window's blocks (sorted by column) are cut where the block
+    column crosses a multiple of `chunk_cols`, and runs longer than
+    `max_blocks` (0: no limit) every `max_blocks` blocks.  Pieces are ordered
+    chunk by chunk, windows in `order` within a chunk, so all SMs read one
+    range of K/V columns at a time.  Returns (pieces int32[P, 4] = (window,
+    first block, end block, slot or -1), splits int32[S, 4] = (window, first
+    slot, pieces, 0), number of slots); a window's pieces own consecutive
+    slots in column order (merged in that order)."""
+    off = np.asarray(window_offsets, dtype=np.int64)
+    cols = np.asarray(block_cols, dtype=np.int64)
+    order = np.asarray(order, dtype=np.int64)
+    if chunk_cols < 1:
+        raise ValueError("chunk_cols must be >= 1")
+    starts, ends = off[order], off[order + 1]
+    counts = ends - starts
+    keep = counts > 0
+    empty_windows = order[~keep]
+    n_blocks = int(counts.sum())
+    item = np.repeat(np.arange(order.shape[0]), counts)           # listed index of every block
+    blk = np.arange(n_blocks) - np.repeat(np.cumsum(counts) - counts, counts) + np.repeat(starts, counts)
+    chunk = cols[blk] // chunk_cols if n_blocks else np.zeros(0, np.int64)
+    first_of_item = np.ones(n_blocks, bool)
+    if n_blocks:
+        first_of_item[1:] = item[1:] != item[:-1]
+    run_start = first_of_item.copy()
+    if n_blocks:
+        run_start[1:] |= chunk[1:] != chunk[:-1]
+    idx = np.arange(n_blocks)
+    if max_blocks and max_blocks > 0 and n_blocks:
+        run_begin = np.maximum.accumulate(np.where(run_start, idx, 0))
+        cut = run_start | ((idx - run_begin) % max_blocks == 0)
+    else:
+        cut = run_start
+    p_start = np.flatnonzero(cut)
+    p_end = np.append(p_start[1:], n_blocks)
+    p_item = item[p_start]
+    p_chunk = chunk[p_start]
+    per_item = np.bincount(p_item, minlength=order.shape[0])
+    split = per_item > 1
+    # slots: consecutive per split window, in the window's column order
+    slot_base = np.cumsum(np.where(split, per_item, 0)) - np.where(split, per_item, 0)
+    rank_in_item = np.arange(p_start.shape[0]) - (np.cumsum(per_item) - per_item)[p_item]
+    p_slot = np.where(split[p_item], slot_base[p_item] + rank_in_item, -1)
+    pieces = np.stack([order[p_item], blk[p_start], blk[p_end - 1] + 1, p_slot], axis=1)
+    sort = np.argsort(p_chunk, kind="stable")
+    pieces = pieces[sort]
+    if empty_windows.size:  # windows without blocks still write zero rows
+        z = np.stack([empty_windows, off[empty_windows], off[empty_windows], -np.ones_like(empty_windows)], axis=1)
+        pieces = np.concatenate([pieces, z])
+    s_items = np.flatnonzero(split)
+    splits = np.stack([order[s_items], slot_base[s_items], per_item[s_items], np.zeros_like(s_items)], axis=1)
+    n_slots = int(per_item[split].sum())
+    return pieces.astype(np.int32).reshape(-1, 4), splits.astype(np.int32).reshape(-1, 4), n_slots
+
+
+def make_chunked_plan(fmt: BlockSparseFormat, heads: int, head_dim: int, order: Optional[torch.Tensor] = None,
+                      chunk_cols: Optional[int] = None, max_blocks: int = 0, l2_fraction: float = 0.5) -> ForwardPlan:
+    """A plan that sweeps the block columns in chunks (column_chunk_pieces),
+    uploaded with f3s_load_plan.  chunk_cols defaults to the number of block
+    columns whose K and V tiles (16 rows x heads x head_dim x 2 B each) fill
+    `l2_fraction` of the device's L2.  Partial states take 64 * heads *
+    (head_dim + 2) bytes per piece of a split window."""
+    lib = _lib.load()
+    device = fmt.window_offsets.device
+    if order is None:
+        order = generate_balanced_window_order(fmt)
+    off, cols = fmt.to_host()
+    order_h = order.cpu().numpy().astype(np.int64)
+    if chunk_cols is None:
+        l2 = torch.cuda.get_device_properties(device).L2_cache_size
+        chunk_cols = max(1, int(l2 * l2_fraction) // (16 * heads * head_dim * 2 * 2))
+    pieces, splits, n_slots = column_chunk_pieces(off, cols, order_h, int(chunk_cols), int(max_blocks))
+    size = lib.f3s_plan_size_for(pieces.shape[0], splits.shape[0], n_slots, heads, head_dim)
+    if size == 0:
+        raise ValueError("unsupported plan parameters")
+    buf = torch.empty(size, dtype=torch.uint8, device=device)
+    pieces = np.ascontiguousarray(pieces)
+    splits = np.ascontiguousarray(splits)
+    off32 = np.ascontiguousarray(off.astype(np.int32))
+    with torch.cuda.device(device):
+        st = lib.f3s_load_plan(pieces.ctypes.data, pieces.shape[0], splits.ctypes.data if splits.size else None,
+                               splits.shape[0], n_slots, off32.ctypes.data, fmt.num_row_windows, heads, head_dim,
+                               _ptr(buf), size, _stream_ptr(device))
+    check(st, "f3s_load_plan")
+    return ForwardPlan(buf, heads, head_dim, int(max_blocks))
+
+
 _OUT_DTYPES = {torch.float32: _lib.F3S_OUT_F32, torch.float16: _lib.F3S_OUT_F16,
                torch.bfloat16: _lib.F3S_OUT_BF16}
 

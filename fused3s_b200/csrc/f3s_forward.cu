@@ -841,7 +841,7 @@ __global__ void __launch_bounds__(256) k_merge_pieces(const PlanHeader* __restri
                 const int hh = row >> 4, r = row & 15;
                 const int node = 16 * sw.x + r;
                 const int64_t srow = (int64_t)node - 16 * (int64_t)q_window_base;
-                if (node < num_nodes && srow < q_rows)
+                if (node < num_nodes && srow >= 0 && srow < q_rows)  // windows outside the slab: never written
                     store_o4(O, (srow * heads + (int64_t)g * hg + hh) * D + 4 * c4, acc[e], o_dtype);
             }
         }
@@ -970,6 +970,75 @@ static int pick_head_group(int heads, int head_dim) {
     int hg = 1;
     while (hg * 2 <= cap && heads % (hg * 2) == 0) hg *= 2;
     return hg;
+}
+
+// A plan whose pieces the caller built (host arrays), e.g. cut at block-column
+// chunk boundaries and ordered chunk by chunk.  Layout: header, pieces,
+// split records, partial states -- the sections the kernels read.
+struct LoadedPlanLayout {
+    size_t pieces, splits, partials, total;
+    int groups, hg;
+};
+
+static LoadedPlanLayout loaded_plan_layout(int num_pieces, int num_split, int num_split_pieces, int heads,
+                                           int head_dim) {
+    LoadedPlanLayout L{};
+    L.hg = pick_head_group(heads, head_dim);
+    L.groups = heads / L.hg;
+    size_t off = sizeof(PlanHeader);
+    L.pieces = off;
+    off = align_up(off + (size_t)std::max(num_pieces, 1) * 16, 256);
+    L.splits = off;
+    off = align_up(off + (size_t)std::max(num_split, 1) * 16, 256);
+    L.partials = off;
+    off = align_up(off + (size_t)std::max(num_split_pieces, 1) * L.groups * L.hg * 16 * (head_dim + 2) * 4, 256);
+    L.total = off;
+    return L;
+}
+
+// Host-side validation keeps every index the kernels derive from the plan
+// inside its buffers: piece ranges inside their window's blocks, partial
+// slots below num_split_pieces, split records inside the slot range.
+int load_plan_impl(const int32_t* pieces, int num_pieces, const int32_t* splits, int num_split,
+                   int num_split_pieces, const int32_t* offsets, int nrw, int heads, int head_dim, void* plan,
+                   size_t plan_bytes, cudaStream_t stream) {
+    if (num_pieces < 0 || num_split < 0 || num_split_pieces < 0 || nrw < 0 || heads <= 0) return F3S_ERR_INVALID_VALUE;
+    if (head_dim != 64 && head_dim != 128) return F3S_ERR_UNSUPPORTED;
+    if (!plan || (num_pieces > 0 && (!pieces || !offsets)) || (num_split > 0 && !splits)) return F3S_ERR_INVALID_VALUE;
+    if ((reinterpret_cast<uintptr_t>(plan) & 255) != 0) return F3S_ERR_INVALID_VALUE;
+    const LoadedPlanLayout L = loaded_plan_layout(num_pieces, num_split, num_split_pieces, heads, head_dim);
+    if (plan_bytes < L.total) return F3S_ERR_WORKSPACE;
+    if ((int64_t)num_pieces * L.groups > INT32_MAX) return F3S_ERR_TOO_LARGE;
+    for (int i = 0; i < num_pieces; ++i) {
+        const int32_t* pc = pieces + 4 * (size_t)i;
+        if (pc[0] < 0 || pc[0] >= nrw || pc[1] < offsets[pc[0]] || pc[2] < pc[1] || pc[2] > offsets[pc[0] + 1] ||
+            pc[3] < -1 || pc[3] >= num_split_pieces)
+            return F3S_ERR_BAD_FORMAT;
+    }
+    for (int i = 0; i < num_split; ++i) {
+        const int32_t* sw = splits + 4 * (size_t)i;
+        if (sw[0] < 0 || sw[0] >= nrw || sw[1] < 0 || sw[2] < 1 || (int64_t)sw[1] + sw[2] > num_split_pieces)
+            return F3S_ERR_BAD_FORMAT;
+    }
+    PlanHeader h{};
+    h.num_pieces = h.max_pieces = num_pieces;
+    h.num_split = h.max_split = num_split;
+    h.num_split_pieces = h.max_split_pieces = num_split_pieces;
+    h.max_blocks = 0;
+    h.heads = heads;
+    h.head_dim = head_dim;
+    h.groups = L.groups;
+    h.hg = L.hg;
+    h.splits_off = (long long)L.splits;
+    h.partials_off = (long long)L.partials;
+    char* base = static_cast<char*>(plan);
+    F3S_CUDA_TRY(cudaMemcpyAsync(base, &h, sizeof(h), cudaMemcpyHostToDevice, stream));
+    if (num_pieces > 0)
+        F3S_CUDA_TRY(cudaMemcpyAsync(base + L.pieces, pieces, (size_t)num_pieces * 16, cudaMemcpyHostToDevice, stream));
+    if (num_split > 0)
+        F3S_CUDA_TRY(cudaMemcpyAsync(base + L.splits, splits, (size_t)num_split * 16, cudaMemcpyHostToDevice, stream));
+    F3S_CUDA_TRY(cudaStreamSynchronize(stream));  // the caller's host arrays may go away on return
+    return F3S_SUCCESS;
 }
 
 int make_plan_impl(const int* offsets, const int* order, int num_items, int64_t num_blocks, int T, int heads,
@@ -1111,6 +1180,20 @@ int f3s_make_plan(const int32_t* d_window_offsets, const int32_t* d_order, int32
                   f3s_stream_t stream) {
     return f3s::make_plan_impl(d_window_offsets, d_order, num_items, num_blocks, max_blocks_per_piece, heads,
                                head_dim, d_plan, plan_bytes, (cudaStream_t)stream);
+}
+
+size_t f3s_plan_size_for(int32_t num_pieces, int32_t num_split, int32_t num_split_pieces, int32_t heads,
+                         int32_t head_dim) {
+    if (num_pieces < 0 || num_split < 0 || num_split_pieces < 0 || heads <= 0) return 0;
+    if (head_dim != 64 && head_dim != 128) return 0;
+    return f3s::loaded_plan_layout(num_pieces, num_split, num_split_pieces, heads, head_dim).total;
+}
+
+int f3s_load_plan(const int32_t* h_pieces, int32_t num_pieces, const int32_t* h_splits, int32_t num_split,
+                  int32_t num_split_pieces, const int32_t* h_window_offsets, int32_t num_row_windows, int32_t heads,
+                  int32_t head_dim, void* d_plan, size_t plan_bytes, f3s_stream_t stream) {
+    return f3s::load_plan_impl(h_pieces, num_pieces, h_splits, num_split, num_split_pieces, h_window_offsets,
+                               num_row_windows, heads, head_dim, d_plan, plan_bytes, (cudaStream_t)stream);
 }
 
 int f3s_forward(const void* d_Q, const void* d_K, const void* d_V, float* d_O, const int32_t* d_window_offsets,

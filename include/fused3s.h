@@ -210,6 +210,30 @@ int f3s_make_plan(const int32_t* d_window_offsets, const int32_t* d_order, int32
                   void* d_plan, size_t plan_bytes, f3s_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * A work plan whose pieces the caller built on the host (no reference
+ * counterpart), for schedules f3s_make_plan does not make -- e.g. windows
+ * cut at block-column chunk boundaries with the pieces ordered chunk by
+ * chunk, so that all SMs read one L2-sized range of K/V at a time.
+ *
+ * h_pieces: int32[4 * num_pieces], per piece in processing order
+ *   (window, first block, end block, partial slot), the block range inside
+ *   the window's [window_offsets[w], window_offsets[w + 1]); slot -1 for a
+ *   window that is one piece, else the slot of its partial state.
+ * h_splits: int32[4 * num_split], per window of several pieces
+ *   (window, first slot, pieces, 0): its pieces own slots first ...
+ *   first + pieces - 1 and are merged in slot order (deterministic).
+ * h_window_offsets: the format's offsets on the host (validation only).
+ * Copies synchronously; every index is validated (F3S_ERR_BAD_FORMAT).
+ * The plan then serves f3s_forward / f3s_forward_ex like one from
+ * f3s_make_plan (d_order / num_items unused).
+ * ---------------------------------------------------------------------- */
+size_t f3s_plan_size_for(int32_t num_pieces, int32_t num_split, int32_t num_split_pieces, int32_t heads,
+                         int32_t head_dim);
+int f3s_load_plan(const int32_t* h_pieces, int32_t num_pieces, const int32_t* h_splits, int32_t num_split,
+                  int32_t num_split_pieces, const int32_t* h_window_offsets, int32_t num_row_windows, int32_t heads,
+                  int32_t head_dim, void* d_plan, size_t plan_bytes, f3s_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * L2 eviction hints for f3s_forward, one per active block (no reference
  * counterpart: a speed hint computed once per graph and window set).
  *

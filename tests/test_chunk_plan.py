@@ -1,0 +1,86 @@
+"""Column-chunked work plans built on the host (column_chunk_pieces):
+against a direct loop, and the invariants the kernels rely on (pieces
+cover every listed window's blocks once, stay inside one column chunk and
+one window, come chunk by chunk; a split window's pieces own consecutive
+slots in column order)."""
+import numpy as np
+import pytest
+
+import oracle
+from fused3s_b200.api import column_chunk_pieces
+from fused3s_b200 import graphs as G
+
+
+def _loop(off, cols, order, cw, T):
+    items = []  # per listed index: list of (chunk, lo, hi)
+    for w in order:
+        b0, b1 = off[w], off[w + 1]
+        ps = []
+        b = b0
+        while b < b1:
+            c = cols[b] // cw
+            e = b
+            while e < b1 and cols[e] // cw == c:
+                e += 1
+            for s in range(b, e, T if T else e - b):
+                ps.append((c, s, min(e, s + T) if T else e))
+            b = e
+        items.append(ps)
+    pieces, splits, slot = [], [], 0
+    slots = []
+    for i, (w, ps) in enumerate(zip(order, items)):
+        if len(ps) > 1:
+            splits.append((w, slot, len(ps), 0))
+            slots.append(list(range(slot, slot + len(ps))))
+            slot += len(ps)
+        else:
+            slots.append([-1] * len(ps))
+    chunks = sorted({c for ps in items for c, _, _ in ps})
+    for c in chunks:
+        for i, (w, ps) in enumerate(zip(order, items)):
+            for k, (cc, lo, hi) in enumerate(ps):
+                if cc == c:
+                    pieces.append((w, lo, hi, slots[i][k]))
+    for w, ps in zip(order, items):
+        if not ps:
+            pieces.append((w, off[w], off[w], -1))
+    return np.array(pieces, np.int32).reshape(-1, 4), np.array(splits, np.int32).reshape(-1, 4), slot
+
+
+@pytest.mark.parametrize("cw,T", [(1, 0), (4, 0), (8, 3), (1000, 0), (3, 1)])
+def test_chunk_pieces_match_loop(cw, T):
+    g = G.powerlaw_graph(num_nodes=1203, directed_edges=9000, max_degree=300, seed=cw + T)
+    off, cols = oracle.convert(g.num_nodes, g.row_ptr, g.col_ind)
+    order = oracle.window_order(off)
+    got = column_chunk_pieces(off, cols, order, cw, T)
+    want = _loop(off, cols, order, cw, T)
+    assert np.array_equal(got[0], want[0]) and np.array_equal(got[1], want[1]) and got[2] == want[2]
+
+
+def test_chunk_pieces_invariants_with_empty_windows_and_subsets():
+    rng = np.random.default_rng(3)
+    n = 16 * 300
+    src = rng.integers(0, n, 20000)
+    src[src // 16 % 7 == 0] = 5  # many windows without blocks
+    g = G.csr_from_edges(n, src, rng.integers(0, n, 20000))
+    off, cols = oracle.convert(n, g.row_ptr, g.col_ind)
+    order = oracle.window_order(off)[::2]  # a subset of the windows
+    pieces, splits, n_slots = column_chunk_pieces(off, cols, order, 16, 5)
+    cw = 16
+    covered = {}
+    for w, lo, hi, s in pieces:
+        assert off[w] <= lo <= hi <= off[w + 1]
+        if hi > lo:
+            assert cols[lo] // cw == cols[hi - 1] // cw and hi - lo <= 5
+        covered.setdefault(w, []).append((lo, hi))
+    assert set(covered) == set(order.tolist())
+    for w, rngs in covered.items():
+        blocks = sorted(b for lo, hi in rngs for b in range(lo, hi))
+        assert blocks == list(range(off[w], off[w + 1]))
+    chunk_seq = [cols[lo] // cw for w, lo, hi, s in pieces if hi > lo]
+    assert chunk_seq == sorted(chunk_seq)
+    used = sorted(s for *_, s in pieces if s >= 0)
+    assert used == list(range(n_slots))
+    for w, first, cnt, _ in splits:
+        mine = sorted((lo, s) for ww, lo, hi, s in pieces if ww == w)
+        assert [s for _, s in mine] == list(range(first, first + cnt))

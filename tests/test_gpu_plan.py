@@ -133,3 +133,68 @@ def test_plan_many_pieces_per_window(lib):
         parity(o, ref, f"T=1 H={heads} d={head_dim}")
         o2 = F.fused3s_forward(Q, K, V, fmt, plan=plan, check_status=True).cpu().numpy()
         assert np.array_equal(o, o2)
+
+
+def test_plan_windows_outside_the_slab_write_nothing_outside_o(lib):
+    """A plan over all windows used with a slab that starts at window 50: the
+    forward reports F3S_ERR_BAD_FORMAT and neither the fused kernel nor the
+    merge writes any row outside O (guard rows around O stay untouched)."""
+    g = G.powerlaw_graph(num_nodes=2003, directed_edges=20000, max_degree=500, seed=21)
+    q, k, v = feats(g.num_nodes, 2, 64)
+    fmt = F.convert_csr_to_block_sparse(g.num_nodes, g.row_ptr, g.col_ind)
+    Q, K, V = gpu(q, k, v)
+    plan = F.make_plan(fmt, 2, 64, max_blocks=4)
+    lo, hi, pad = 50, 100, 64
+    r0, r1 = 16 * lo, 16 * hi
+    big = torch.full((r1 - r0 + 2 * pad, 2, 64), 7.0, dtype=torch.float32, device="cuda")
+    out = big[pad:pad + r1 - r0]
+    with pytest.raises(_lib.Fused3SError) as e:
+        F.fused3s_forward(Q[r0:r1].contiguous(), K, V, fmt, plan=plan, out=out, q_window_base=lo,
+                          check_status=True)
+    assert e.value.status == _lib.F3S_ERR_BAD_FORMAT
+    torch.cuda.synchronize()
+    assert torch.all(big[:pad] == 7.0) and torch.all(big[pad + r1 - r0:] == 7.0)
+
+
+@pytest.mark.parametrize("heads,head_dim,cw,T", [(2, 64, 8, 0), (8, 64, 4, 5), (4, 128, 16, 0), (1, 64, 2, 3)])
+def test_column_chunked_plan_matches_oracle(lib, heads, head_dim, cw, T):
+    """Host-built column-chunked plans (f3s_load_plan): same parity bar,
+    deterministic, and equal to themselves on a window subset's slab."""
+    g = G.powerlaw_graph(num_nodes=2003, directed_edges=20000, max_degree=500, seed=heads + cw)
+    q, k, v = feats(g.num_nodes, heads, head_dim)
+    fmt = F.convert_csr_to_block_sparse(g.num_nodes, g.row_ptr, g.col_ind)
+    plan = F.make_chunked_plan(fmt, heads, head_dim, chunk_cols=cw, max_blocks=T)
+    Q, K, V = gpu(q, k, v)
+    o = F.fused3s_forward(Q, K, V, fmt, plan=plan, check_status=True).cpu().numpy()
+    off, cols = fmt.to_host()
+    ref = oracle.block_attention(g.num_nodes, q.astype(np.float32), k.astype(np.float32), v.astype(np.float32),
+                                 off, cols, threads=8)
+    parity(o, ref, f"chunked H={heads} d={head_dim} cw={cw} T={T}")
+    o2 = F.fused3s_forward(Q, K, V, fmt, plan=plan, check_status=True).cpu().numpy()
+    assert np.array_equal(o, o2)
+    # a slab of windows [30, 90) with its own chunked plan: the same rows bit for bit
+    lo, hi = 30, 90
+    order = F.generate_balanced_window_order(fmt)
+    mine = order[(order >= lo) & (order < hi)].contiguous()
+    sp = F.make_chunked_plan(fmt, heads, head_dim, order=mine, chunk_cols=cw, max_blocks=T)
+    r0, r1 = 16 * lo, 16 * hi
+    os_ = F.fused3s_forward(Q[r0:r1].contiguous(), K, V, fmt, plan=sp, q_window_base=lo, check_status=True)
+    assert np.array_equal(os_.cpu().numpy(), o[r0:r1])
+
+
+def test_load_plan_rejects_out_of_range_pieces(lib):
+    g = G.make_graph("c1")
+    fmt = F.convert_csr_to_block_sparse(g.num_nodes, g.row_ptr, g.col_ind)
+    off, cols = fmt.to_host()
+    pieces, splits, n_slots = F.column_chunk_pieces(off, cols, np.arange(fmt.num_row_windows), 8, 0)
+    size = lib.f3s_plan_size_for(pieces.shape[0], splits.shape[0], n_slots, 1, 64)
+    buf = torch.empty(size, dtype=torch.uint8, device="cuda")
+    off32 = np.ascontiguousarray(off.astype(np.int32))
+    stream = torch.cuda.current_stream().cuda_stream
+    for bad in ((0, 2, 10**6), (0, 3, n_slots), (0, 0, fmt.num_row_windows)):
+        p = pieces.copy()
+        p[bad[0], bad[1]] = bad[2]
+        p = np.ascontiguousarray(p)
+        st = lib.f3s_load_plan(p.ctypes.data, p.shape[0], np.ascontiguousarray(splits).ctypes.data, splits.shape[0],
+                               n_slots, off32.ctypes.data, fmt.num_row_windows, 1, 64, buf.data_ptr(), size, stream)
+        assert st == _lib.F3S_ERR_BAD_FORMAT
