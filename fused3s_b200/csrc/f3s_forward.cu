@@ -20,8 +20,8 @@
 //     head-chunks, HA odd, and one of the remaining chunk.  In shared memory
 //     the tile is node-major with a node stride of HA * 128 B, an odd
 //     multiple of the swizzle row, so ldmatrix reads are conflict-free
-//     (chunk_row()).  The K and V boxes of a block are issued by separate
-//     lanes of the producer warp in one instruction.
+//     (chunk_row()).  Up to 32 blocks are issued per round, one per lane of
+//     the producer warp; each lane issues its block's K and V boxes.
 //   * L2 eviction priority per load: Q tiles (read once) evict-first; K/V
 //     tiles by the caller's per-block hint, the hint of the block's column
 //     (popular columns evict-last, columns used by one window evict-first).
@@ -256,9 +256,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------ producer --
         // The whole warp runs this loop.  A block's K and V tiles are NBOX
-        // boxes each; lanes [0, NBOX) issue the K boxes and lanes
-        // [NBOX, 2*NBOX) the V boxes in one warp instruction (lanes
-        // [0, NBOX) also issue a window's Q boxes).
+        // boxes each, issued by the lane that claimed the block (rounds of
+        // up to ISSUE_W blocks below); lanes [0, NBOX) issue a window's Q
+        // boxes.
         if (lane == 0) {
             tma_prefetch_desc(&maps.qa);
             tma_prefetch_desc(&maps.qb);
