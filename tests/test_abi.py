@@ -87,3 +87,17 @@ def test_text_pieces_cut_at_separators():
         assert np.array_equal(joined, vals)
     with pytest.raises(ValueError):
         text_pieces(np.frombuffer(b"123456789 1", dtype=np.uint8), 4)
+
+
+def test_c_usage_compiles_as_plain_c():
+    """The documented C call sequence compiles against include/fused3s.h with
+    a C compiler (the header stays plain C, every call matches its
+    declaration)."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    r = subprocess.run([gcc, "-std=c11", "-Wall", "-Werror", "-fsyntax-only", f"-I{ROOT / 'include'}",
+                        str(ROOT / "tests" / "cpp" / "c_abi_usage.c")], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
