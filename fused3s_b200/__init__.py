@@ -21,7 +21,12 @@ from .api import (
     load_csr_graph,
     load_csr_graph_device,
     column_chunk_pieces,
+    column_slices,
+    forward_pieces,
+    load_plan,
     make_chunked_plan,
+    make_sliced_plan,
+    plan_merge,
     make_plan,
     parse_int32_text,
     workspace_status,
@@ -40,6 +45,11 @@ __all__ = [
     "make_plan",
     "make_chunked_plan",
     "column_chunk_pieces",
+    "column_slices",
+    "forward_pieces",
+    "load_plan",
+    "make_sliced_plan",
+    "plan_merge",
     "float2half",
     "forward_workspace",
     "fused3s_forward",

@@ -61,6 +61,9 @@ SIGNATURES = {
     "f3s_plan_size_for": (_SZ, [_I32, _I32, _I32, _I32, _I32]),
     "f3s_load_plan": (ctypes.c_int, [_P, _I32, _P, _I32, _I32, _P, _I32, _I32, _I32, _P, _SZ, _P]),
     "f3s_make_plan": (ctypes.c_int, [_P, _P, _I32, _I64, _I32, _I32, _I32, _P, _SZ, _P]),
+    "f3s_forward_pieces": (ctypes.c_int, [_P, _P, _P, _P, _I32, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
+                                          _I32, _I32, _I32, _P, _SZ, _P]),
+    "f3s_plan_merge": (ctypes.c_int, [_P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P]),
     "f3s_block_hints_workspace_size": (_SZ, [_I32]),
     "f3s_block_hints": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I64, _I64, _P, _P, _SZ, _P]),
     "f3s_1tb1rw_launch": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _P]),

@@ -300,11 +300,14 @@ def block_hints(fmt: BlockSparseFormat, heads: int, head_dim: int, order: Option
 @dataclasses.dataclass
 class ForwardPlan:
     """Device-resident work plan (f3s_make_plan): the listed windows in
-    order, heavy ones cut into pieces of at most `max_blocks` blocks."""
+    order, heavy ones cut into pieces of at most `max_blocks` blocks.
+    piece_ranges: for a plan cut at K / V slice boundaries (make_sliced_plan),
+    the [begin, end) pieces of each slice."""
     buffer: torch.Tensor
     heads: int
     head_dim: int
     max_blocks: int
+    piece_ranges: Optional[list] = None
 
 
 def auto_piece_blocks(num_blocks: int, device=None) -> int:
@@ -346,23 +349,36 @@ def make_plan(fmt: BlockSparseFormat, heads: int, head_dim: int, order: Optional
     return ForwardPlan(buf, heads, head_dim, int(max_blocks))
 
 
-def column_chunk_pieces(window_offsets: np.ndarray, block_cols: np.ndarray, order: np.ndarray, chunk_cols: int,
-                        max_blocks: int = 0):
+def column_chunk_pieces(window_offsets: np.ndarray, block_cols: np.ndarray, order: np.ndarray, chunk_cols: int = 0,
+                        max_blocks: int = 0, col_cuts=None):
     """Pieces of a column-chunked plan, built on the host.
 
     Every listed window's blocks (sorted by column) are cut where the block
-    column crosses a multiple of `chunk_cols`, and runs longer than
-    `max_blocks` (0: no limit) every `max_blocks` blocks.  Pieces are ordered
-    chunk by chunk, windows in `order` within a chunk, so all SMs read one
-    range of K/V columns at a time.  Returns (pieces int32[P, 4] = (window,
-    first block, end block, slot or -1), splits int32[S, 4] = (window, first
-    slot, pieces, 0), number of slots); a window's pieces own consecutive
-    slots in column order (merged in that order)."""
+    column crosses a chunk boundary -- a multiple of `chunk_cols`, or the
+    explicit ascending boundaries `col_cuts` (first 0, last >= the number of
+    block columns) -- and runs longer than `max_blocks` (0: no limit) every
+    `max_blocks` blocks.  Pieces are ordered chunk by chunk, windows in
+    `order` within a chunk, so all SMs read one range of K/V columns at a
+    time.  Returns (pieces int32[P, 4] = (window, first block, end block, slot
+    or -1), splits int32[S, 4] = (window, first slot, pieces, 0), number of
+    slots, chunk_starts int64[C + 1]): the pieces of chunk c are rows
+    chunk_starts[c] ... chunk_starts[c + 1] - 1; a window without blocks is
+    one empty piece in chunk 0.  A window's pieces own consecutive slots in
+    column order (merged in that order)."""
     off = np.asarray(window_offsets, dtype=np.int64)
     cols = np.asarray(block_cols, dtype=np.int64)
     order = np.asarray(order, dtype=np.int64)
-    if chunk_cols < 1:
-        raise ValueError("chunk_cols must be >= 1")
+    if col_cuts is None:
+        if chunk_cols < 1:
+            raise ValueError("chunk_cols must be >= 1")
+        n_cols = off.shape[0] - 1
+        col_cuts = np.arange(0, n_cols + chunk_cols, chunk_cols, dtype=np.int64)
+        if col_cuts.shape[0] < 2:
+            col_cuts = np.array([0, max(chunk_cols, 1)], np.int64)
+    col_cuts = np.asarray(col_cuts, dtype=np.int64)
+    if col_cuts.ndim != 1 or col_cuts.shape[0] < 2 or col_cuts[0] != 0 or np.any(np.diff(col_cuts) < 0):
+        raise ValueError("col_cuts must be ascending boundaries starting at 0")
+    n_chunks = col_cuts.shape[0] - 1
     starts, ends = off[order], off[order + 1]
     counts = ends - starts
     keep = counts > 0
@@ -370,7 +386,9 @@ def column_chunk_pieces(window_offsets: np.ndarray, block_cols: np.ndarray, orde
     n_blocks = int(counts.sum())
     item = np.repeat(np.arange(order.shape[0]), counts)           # listed index of every block
     blk = np.arange(n_blocks) - np.repeat(np.cumsum(counts) - counts, counts) + np.repeat(starts, counts)
-    chunk = cols[blk] // chunk_cols if n_blocks else np.zeros(0, np.int64)
+    chunk = (np.searchsorted(col_cuts, cols[blk], side="right") - 1) if n_blocks else np.zeros(0, np.int64)
+    if n_blocks and (chunk.min() < 0 or chunk.max() >= n_chunks):
+        raise ValueError("col_cuts do not cover every block column")
     first_of_item = np.ones(n_blocks, bool)
     if n_blocks:
         first_of_item[1:] = item[1:] != item[:-1]
@@ -393,16 +411,20 @@ def column_chunk_pieces(window_offsets: np.ndarray, block_cols: np.ndarray, orde
     slot_base = np.cumsum(np.where(split, per_item, 0)) - np.where(split, per_item, 0)
     rank_in_item = np.arange(p_start.shape[0]) - (np.cumsum(per_item) - per_item)[p_item]
     p_slot = np.where(split[p_item], slot_base[p_item] + rank_in_item, -1)
-    pieces = np.stack([order[p_item], blk[p_start], blk[p_end - 1] + 1, p_slot], axis=1)
-    sort = np.argsort(p_chunk, kind="stable")
-    pieces = pieces[sort]
-    if empty_windows.size:  # windows without blocks still write zero rows
+    pieces = np.stack([order[p_item], blk[p_start], blk[p_end - 1] + 1, p_slot], axis=1).reshape(-1, 4)
+    if empty_windows.size:  # windows without blocks still write zero rows (chunk 0)
         z = np.stack([empty_windows, off[empty_windows], off[empty_windows], -np.ones_like(empty_windows)], axis=1)
         pieces = np.concatenate([pieces, z])
+        p_chunk = np.concatenate([p_chunk, np.zeros(empty_windows.shape[0], np.int64)])
+    sort = np.argsort(p_chunk, kind="stable")
+    pieces = pieces[sort]
+    chunk_starts = np.zeros(n_chunks + 1, np.int64)
+    np.cumsum(np.bincount(p_chunk, minlength=n_chunks)[:n_chunks], out=chunk_starts[1:])
     s_items = np.flatnonzero(split)
     splits = np.stack([order[s_items], slot_base[s_items], per_item[s_items], np.zeros_like(s_items)], axis=1)
     n_slots = int(per_item[split].sum())
-    return pieces.astype(np.int32).reshape(-1, 4), splits.astype(np.int32).reshape(-1, 4), n_slots
+    return (pieces.astype(np.int32).reshape(-1, 4), splits.astype(np.int32).reshape(-1, 4), n_slots,
+            chunk_starts)
 
 
 def make_chunked_plan(fmt: BlockSparseFormat, heads: int, head_dim: int, order: Optional[torch.Tensor] = None,
@@ -421,20 +443,59 @@ def make_chunked_plan(fmt: BlockSparseFormat, heads: int, head_dim: int, order: 
     if chunk_cols is None:
         l2 = torch.cuda.get_device_properties(device).L2_cache_size
         chunk_cols = max(1, int(l2 * l2_fraction) // (16 * heads * head_dim * 2 * 2))
-    pieces, splits, n_slots = column_chunk_pieces(off, cols, order_h, int(chunk_cols), int(max_blocks))
-    size = lib.f3s_plan_size_for(pieces.shape[0], splits.shape[0], n_slots, heads, head_dim)
+    pieces, splits, n_slots, _ = column_chunk_pieces(off, cols, order_h, int(chunk_cols), int(max_blocks))
+    return load_plan(fmt, pieces, splits, n_slots, heads, head_dim, off_host=off, max_blocks=int(max_blocks))
+
+
+def load_plan(fmt: BlockSparseFormat, pieces: np.ndarray, splits: np.ndarray, n_slots: int, heads: int,
+              head_dim: int, off_host: Optional[np.ndarray] = None, max_blocks: int = 0,
+              piece_ranges=None) -> ForwardPlan:
+    """Upload a host-built plan (f3s_load_plan, validated on the host)."""
+    lib = _lib.load()
+    device = fmt.window_offsets.device
+    off = fmt.window_offsets.cpu().numpy() if off_host is None else off_host
+    pieces = np.ascontiguousarray(pieces, dtype=np.int32).reshape(-1, 4)
+    splits = np.ascontiguousarray(splits, dtype=np.int32).reshape(-1, 4)
+    size = lib.f3s_plan_size_for(pieces.shape[0], splits.shape[0], int(n_slots), heads, head_dim)
     if size == 0:
         raise ValueError("unsupported plan parameters")
     buf = torch.empty(size, dtype=torch.uint8, device=device)
-    pieces = np.ascontiguousarray(pieces)
-    splits = np.ascontiguousarray(splits)
     off32 = np.ascontiguousarray(off.astype(np.int32))
     with torch.cuda.device(device):
         st = lib.f3s_load_plan(pieces.ctypes.data, pieces.shape[0], splits.ctypes.data if splits.size else None,
-                               splits.shape[0], n_slots, off32.ctypes.data, fmt.num_row_windows, heads, head_dim,
-                               _ptr(buf), size, _stream_ptr(device))
+                               splits.shape[0], int(n_slots), off32.ctypes.data, fmt.num_row_windows, heads,
+                               head_dim, _ptr(buf), size, _stream_ptr(device))
     check(st, "f3s_load_plan")
-    return ForwardPlan(buf, heads, head_dim, int(max_blocks))
+    return ForwardPlan(buf, heads, head_dim, int(max_blocks), piece_ranges)
+
+
+def column_slices(num_nodes: int, parts: int):
+    """K / V cut into `parts` slices of whole block columns: boundaries
+    col_cuts[0] = 0 < ... < col_cuts[parts] = ceil(num_nodes / 16) (equal
+    sizes up to one block column), and each slice's node rows [r0, r1)."""
+    nrw = (num_nodes + 15) // 16
+    cuts = np.array([(nrw * j) // parts for j in range(parts + 1)], np.int64)
+    rows = [(min(16 * int(a), num_nodes), min(16 * int(b), num_nodes)) for a, b in zip(cuts[:-1], cuts[1:])]
+    return cuts, rows
+
+
+def make_sliced_plan(fmt: BlockSparseFormat, heads: int, head_dim: int, col_cuts, order: Optional[torch.Tensor] = None,
+                     max_blocks: int = 0) -> ForwardPlan:
+    """A plan for K / V held in slices of block columns (col_cuts, e.g. from
+    column_slices): every listed window is cut at the slice boundaries, and
+    the pieces of slice j are plan.piece_ranges[j] -- run them with
+    forward_pieces(..., kv_col_base=col_cuts[j]) on that slice's K / V rows,
+    in any slice order, then plan_merge once."""
+    device = fmt.window_offsets.device
+    if order is None:
+        order = generate_balanced_window_order(fmt)
+    off, cols = fmt.to_host()
+    order_h = order.cpu().numpy().astype(np.int64)
+    pieces, splits, n_slots, starts = column_chunk_pieces(off, cols, order_h, max_blocks=int(max_blocks),
+                                                          col_cuts=col_cuts)
+    ranges = [(int(a), int(b)) for a, b in zip(starts[:-1], starts[1:])]
+    return load_plan(fmt, pieces, splits, n_slots, heads, head_dim, off_host=off, max_blocks=int(max_blocks),
+                     piece_ranges=ranges)
 
 
 _OUT_DTYPES = {torch.float32: _lib.F3S_OUT_F32, torch.float16: _lib.F3S_OUT_F16,
@@ -497,6 +558,51 @@ def fused3s_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: Bloc
         check(st, "f3s_forward_ex")
         if check_status:
             check(lib.f3s_workspace_status(_ptr(ws), _stream_ptr(device)), "f3s_forward (device)")
+    return out
+
+
+def forward_pieces(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: BlockSparseFormat, plan: ForwardPlan,
+                   out: torch.Tensor, piece_begin: int = 0, piece_end: int = -1, kv_col_base: int = 0,
+                   q_window_base: int = 0, block_hints: Optional[torch.Tensor] = None,
+                   check_status: bool = False) -> torch.Tensor:
+    """Pieces [piece_begin, piece_end) of `plan` (f3s_forward_pieces), with
+    K / V holding only the graph's rows 16 * kv_col_base ... (K.shape[0]
+    rows): windows of one piece get their O rows, split windows' pieces
+    leave partial states in the plan for plan_merge.  No merge here."""
+    lib = _lib.load()
+    _check_features(Q, K, V)
+    q3, k3 = _as_nhd(Q), _as_nhd(K)
+    q_rows, heads, head_dim = q3.shape
+    if k3.shape[1:] != (heads, head_dim) or (plan.heads, plan.head_dim) != (heads, head_dim):
+        raise ValueError("Q, K, V and the plan must agree on heads and head_dim")
+    if out.shape != Q.shape or not out.is_contiguous() or out.dtype not in _OUT_DTYPES:
+        raise ValueError("out must be a contiguous float32/float16/bfloat16 tensor shaped like Q")
+    device = Q.device
+    ws = _WS.get(device, "forward", lib.f3s_forward_workspace_size())
+    with torch.cuda.device(device):
+        st = lib.f3s_forward_pieces(_ptr(Q), _ptr(K), _ptr(V), _ptr(out), _OUT_DTYPES[out.dtype],
+                                    _ptr(fmt.window_offsets), fmt.cols_ptr, _ptr(block_hints), _ptr(plan.buffer),
+                                    int(piece_begin), int(piece_end), int(kv_col_base), int(k3.shape[0]),
+                                    fmt.num_nodes, heads, head_dim, int(q_window_base), q_rows, _ptr(ws),
+                                    ws.numel(), _stream_ptr(device))
+        check(st, "f3s_forward_pieces")
+        if check_status:
+            check(lib.f3s_workspace_status(_ptr(ws), _stream_ptr(device)), "f3s_forward_pieces (device)")
+    return out
+
+
+def plan_merge(plan: ForwardPlan, out: torch.Tensor, num_nodes: int, q_window_base: int = 0) -> torch.Tensor:
+    """Writes the O rows of the plan's split windows from their partial
+    states (f3s_plan_merge), after every piece ran."""
+    lib = _lib.load()
+    o3 = _as_nhd(out)
+    if out.dtype not in _OUT_DTYPES or not out.is_contiguous():
+        raise ValueError("out must be a contiguous float32/float16/bfloat16 tensor")
+    device = out.device
+    with torch.cuda.device(device):
+        st = lib.f3s_plan_merge(_ptr(plan.buffer), _ptr(out), _OUT_DTYPES[out.dtype], int(num_nodes), plan.heads,
+                                plan.head_dim, int(q_window_base), o3.shape[0], _stream_ptr(device))
+    check(st, "f3s_plan_merge")
     return out
 
 

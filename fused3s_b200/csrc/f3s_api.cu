@@ -1,7 +1,11 @@
 // f3s_api.cu -- C-ABI glue of libfused3s.so: status strings, the workspace
-// status read-back, the reference-signature launch and the fp32 -> fp16 cast.
+// status read-back, the reference-signature launch, the fp32 -> fp16 cast and
+// the per-context bookkeeping the other translation units share.
 #include <atomic>
+#include <map>
 #include <mutex>
+#include <utility>
+#include <cuda.h>
 #include "f3s_internal.cuh"
 
 namespace f3s {
@@ -11,50 +15,83 @@ static std::atomic<int> g_last_cuda_error{0};
 void note_cuda_error(cudaError_t e) { g_last_cuda_error.store((int)e); }
 
 int num_sms_of_current_device() {
-    static int cache[64] = {};
+    static std::atomic<int> cache[kMaxDevices] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 1;
-    if (dev < 64 && cache[dev] > 0) return cache[dev];
+    if (dev >= 0 && dev < kMaxDevices) {
+        const int c = cache[dev].load(std::memory_order_relaxed);
+        if (c > 0) return c;
+    }
     int n = 1;
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) n = 1;
-    if (dev < 64) cache[dev] = n;
+    if (dev >= 0 && dev < kMaxDevices) cache[dev].store(n, std::memory_order_relaxed);
     return n;
 }
 
-int forward_impl(const void* Q, const void* K, const void* V, void* O, int o_dtype, const int* offsets,
-                 const int* cols, const int* order, const uint8_t* block_hints, const void* plan, int num_items,
-                 int num_nodes, int heads, int head_dim, int q_window_base, int q_rows, void* ws, size_t ws_bytes,
-                 cudaStream_t stream, uint64_t timeout_ns);
+// Driver entry points for the context identity, looked up once through the
+// runtime (the library links no libcuda).
+using PfnCtxGetCurrent = CUresult (*)(CUcontext*);
+using PfnCtxGetId = CUresult (*)(CUcontext, unsigned long long*);
 
-// Library-owned forward workspace for the reference-signature launch, one
-// per device, allocated on first use and kept until process exit.
-static void* legacy_workspace(int* rc) {
-    static void* ws[64] = {};
-    static std::mutex mu;
+int current_context(ContextKey* key) {
+    static PfnCtxGetCurrent get_current = nullptr;
+    static PfnCtxGetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<PfnCtxGetCurrent>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<PfnCtxGetId>(p);
+    });
     int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess || dev >= 64) {
+    F3S_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return F3S_ERR_UNSUPPORTED;
+    if (!get_current || !get_id) return F3S_ERR_CUDA;
+    CUcontext ctx = nullptr;
+    if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) {
+        // no context current on this thread yet: cudaSetDevice makes the
+        // device's primary context current (creating it if needed)
+        F3S_CUDA_TRY(cudaSetDevice(dev));
+        if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return F3S_ERR_CUDA;
+    }
+    unsigned long long id = 0;
+    if (get_id(ctx, &id) != CUDA_SUCCESS) return F3S_ERR_CUDA;
+    key->device = dev;
+    key->id = id;
+    return F3S_SUCCESS;
+}
+
+
+// Library-owned forward workspaces for the reference-signature launch, one
+// per (context, stream): the launch's ticket counter and status word live
+// there, so launches on different streams never share them.  Allocated on
+// first use of a stream and kept until the process exits (256 bytes each);
+// entries of a destroyed context are never matched again.
+static void* legacy_workspace(cudaStream_t stream, int* rc) {
+    static std::map<std::pair<unsigned long long, uintptr_t>, void*> ws;
+    static std::mutex mu;
+    ContextKey k{};
+    *rc = current_context(&k);
+    if (*rc != F3S_SUCCESS) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_pair(k.id, reinterpret_cast<uintptr_t>(stream));
+    auto it = ws.find(key);
+    if (it != ws.end()) return it->second;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, kWsHeaderBytes);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, kWsHeaderBytes);
+    if (e != cudaSuccess) {
         note_cuda_error(e);
         *rc = F3S_ERR_CUDA;
         return nullptr;
     }
-    std::lock_guard<std::mutex> lock(mu);
-    if (!ws[dev]) {
-        e = cudaMalloc(&ws[dev], kWsHeaderBytes);
-        if (e != cudaSuccess) {
-            note_cuda_error(e);
-            *rc = F3S_ERR_CUDA;
-            return nullptr;
-        }
-        e = cudaMemset(ws[dev], 0, kWsHeaderBytes);
-        if (e != cudaSuccess) {
-            note_cuda_error(e);
-            *rc = F3S_ERR_CUDA;
-            return nullptr;
-        }
-    }
-    *rc = F3S_SUCCESS;
-    return ws[dev];
+    ws[key] = p;
+    return p;
 }
 
 __global__ void k_half_from_float(const float* __restrict__ in, __half* __restrict__ out, int64_t n) {
@@ -104,14 +141,15 @@ int f3s_workspace_status(void* d_workspace, f3s_stream_t stream) {
 int f3s_1tb1rw_launch(const void* Q, const void* K, const void* V, float* O_out, const int32_t* window_offsets,
                       const int32_t* block_col_indices, const int32_t* window_order, int32_t num_row_windows,
                       int32_t feat_dim, f3s_stream_t stream) {
+    f3s::NvtxRange nvtx_("f3s_1tb1rw_launch");
     if (num_row_windows < 0 || (int64_t)num_row_windows * 16 > INT32_MAX) return F3S_ERR_INVALID_VALUE;
     int rc = 0;
-    void* ws = f3s::legacy_workspace(&rc);
+    void* ws = f3s::legacy_workspace((cudaStream_t)stream, &rc);
     if (!ws) return rc;
     const int rows = num_row_windows * 16;
     return f3s::forward_impl(Q, K, V, O_out, F3S_OUT_F32, window_offsets, block_col_indices, window_order, nullptr,
                              nullptr, num_row_windows, rows, 1, feat_dim, 0, rows, ws, f3s::kWsHeaderBytes,
-                             (cudaStream_t)stream, 10ull * 1000 * 1000 * 1000);
+                             (cudaStream_t)stream, 10ull * 1000 * 1000 * 1000, f3s::PieceRange{});
 }
 
 int f3s_half_from_float(const float* d_in, void* d_out, int64_t n, f3s_stream_t stream) {

@@ -334,19 +334,19 @@ static int convert_impl(const int32_t* d_row_ptr, const int32_t* d_col_ind, int3
         F3S_LAUNCH_CHECK();
         const int bits = std::min(nrw, kHeavyBitmapBits);
         const size_t smem = (size_t)((bits + 31) / 32) * 4;
-        static bool attr_set[64] = {};
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (dev < 64 && !attr_set[dev]) {
+        // the bitmap kernel's shared-memory attribute, once per CUDA context
+        static PerContext<int> attr_once;
+        int rc = attr_once.get(nullptr, [](int*) -> int {
             F3S_CUDA_TRY(cudaFuncSetAttribute(k_convert_heavy, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               (kHeavyBitmapBits / 32) * 4));
-            attr_set[dev] = true;
-        }
+            return F3S_SUCCESS;
+        });
+        if (rc != F3S_SUCCESS) return rc;
         const int grid = std::max(1, std::min(nrw, num_sms_of_current_device()));
         k_convert_heavy<<<grid, kHeavyThreads, smem, stream>>>(d_row_ptr, d_col_ind, num_nodes, nrw, tmp,
                                                                counts, heavy, hdr, bits);
         F3S_LAUNCH_CHECK();
-        int rc = device_exclusive_scan(counts, d_window_offsets, nrw, true, tiles, stream);
+        rc = device_exclusive_scan(counts, d_window_offsets, nrw, true, tiles, stream);
         if (rc != F3S_SUCCESS) return rc;
         k_convert_compact<<<(nrw + 7) / 8, 256, 0, stream>>>(d_row_ptr, nrw, tmp, d_window_offsets,
                                                              d_block_cols);
@@ -660,28 +660,20 @@ constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
+// The array's device address in the current context, looked up with the
+// device current the first time a context uses it (and again after a device
+// reset, whose new context places the array anew).
 static int noalloc_scratch_address(void** out) {
-    static void* addr[64] = {};
-    static std::mutex mu;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) {
-        note_cuda_error(e);
-        return F3S_ERR_CUDA;
-    }
-    if (dev < 0 || dev >= 64) return F3S_ERR_UNSUPPORTED;
-    std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
-        void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || p == nullptr) {
+    static PerContext<void*> addr;
+    return addr.get(out, [](void** p) -> int {
+        *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(p, g_noalloc_scratch);
+        if (e != cudaSuccess || *p == nullptr) {
             note_cuda_error(e);
             return F3S_ERR_CUDA;
         }
-        addr[dev] = p;
-    }
-    *out = addr[dev];
-    return F3S_SUCCESS;
+        return F3S_SUCCESS;
+    });
 }
 
 static int convert_noalloc_impl(const int32_t* d_row_ptr, const int32_t* d_col_ind, int32_t num_nodes,
@@ -708,6 +700,7 @@ extern "C" {
 int f3s_convert_noalloc(const int32_t* d_row_ptr, const int32_t* d_col_ind, int32_t num_nodes, int64_t nnz,
                         int32_t* d_window_offsets, int32_t* d_block_cols, int64_t* h_num_blocks,
                         f3s_stream_t stream) {
+    f3s::NvtxRange nvtx_("f3s_convert_noalloc");
     return f3s::convert_noalloc_impl(d_row_ptr, d_col_ind, num_nodes, nnz, d_window_offsets, d_block_cols,
                                      h_num_blocks, (cudaStream_t)stream);
 }
@@ -720,6 +713,7 @@ size_t f3s_convert_workspace_size(int32_t num_nodes, int64_t nnz) {
 int f3s_convert(const int32_t* d_row_ptr, const int32_t* d_col_ind, int32_t num_nodes, int64_t nnz,
                 int32_t* d_window_offsets, int32_t* d_block_cols, void* d_workspace, size_t workspace_bytes,
                 int64_t* h_num_blocks, f3s_stream_t stream) {
+    f3s::NvtxRange nvtx_("f3s_convert");
     return f3s::convert_impl(d_row_ptr, d_col_ind, num_nodes, nnz, d_window_offsets, d_block_cols,
                              d_workspace, workspace_bytes, h_num_blocks, (cudaStream_t)stream);
 }
@@ -732,6 +726,7 @@ size_t f3s_block_hints_workspace_size(int32_t num_row_windows) {
 int f3s_block_hints(const int32_t* d_window_offsets, const int32_t* d_block_cols, const int32_t* d_order,
                     int32_t num_items, int32_t num_row_windows, int64_t bytes_per_column, int64_t l2_budget_bytes,
                     uint8_t* d_block_hints, void* d_workspace, size_t workspace_bytes, f3s_stream_t stream) {
+    f3s::NvtxRange nvtx_("f3s_block_hints");
     return f3s::block_hints_impl(d_window_offsets, d_block_cols, d_order, num_items, num_row_windows,
                                  bytes_per_column, l2_budget_bytes, d_block_hints, d_workspace, workspace_bytes,
                                  (cudaStream_t)stream);
@@ -744,6 +739,7 @@ size_t f3s_window_order_workspace_size(int32_t num_row_windows) {
 
 int f3s_window_order(const int32_t* d_window_offsets, int32_t num_row_windows, int32_t* d_order,
                      void* d_workspace, size_t workspace_bytes, f3s_stream_t stream) {
+    f3s::NvtxRange nvtx_("f3s_window_order");
     return f3s::window_order_impl(d_window_offsets, num_row_windows, d_order, d_workspace, workspace_bytes,
                                   (cudaStream_t)stream);
 }

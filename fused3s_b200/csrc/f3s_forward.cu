@@ -43,6 +43,7 @@
 //     status word in the workspace instead of hanging.
 #include <algorithm>
 #include <mutex>
+#include <vector>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
@@ -138,6 +139,10 @@ struct FwdParams {
     int tail;           // N % 16 (0: no masked column)
     const uint8_t* hints;  // per block L2 hint (1 keep, 2 stream, else normal) or null
     int o_dtype;           // f3s_out_dtype of O
+    int piece_begin;       // with a plan: first piece of this launch
+    int piece_end;         // with a plan: end of the launch's pieces, or -1 for all
+    int kv_col_base;       // first block column held in K / V (row 16 * kv_col_base of the graph)
+    int kv_cols;           // block columns held in K / V
 };
 
 // O stores: fp32 as computed, or rounded to nearest into fp16 / bf16.
@@ -274,9 +279,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         int n_units = p.num_items;
         const int4* pieces = nullptr;  // plan pieces (w, b0, b1, partial slot or -1)
         if (p.plan != nullptr) {
-            pieces = reinterpret_cast<const int4*>(p.plan + 1);
-            n_units = p.plan->num_pieces;
-            if (p.plan->status != 0 || p.plan->heads != p.heads || p.plan->head_dim != D) {
+            // this launch's range of the plan's pieces
+            const int np_all = p.plan->num_pieces;
+            const int pe = p.piece_end < 0 ? np_all : p.piece_end;
+            pieces = reinterpret_cast<const int4*>(p.plan + 1) + p.piece_begin;
+            n_units = pe - p.piece_begin;
+            if (p.plan->status != 0 || p.plan->heads != p.heads || p.plan->head_dim != D || pe > np_all ||
+                n_units < 0) {
                 if (lane == 0) raise_error(err, F3S_ERR_BAD_FORMAT);
                 n_units = 0;
             }
@@ -372,7 +381,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 const bool more = nbase + lane < b1;
                 const int nc = more ? __ldg(p.cols + nbase + lane) : 0;
                 const int nh = (more && p.hints != nullptr) ? (int)__ldg(p.hints + nbase + lane) : 0;
-                if (__any_sync(0xffffffffu, lane < n && (myc < 0 || myc >= p.nrw_total))) {
+                // every block column must lie in the K / V rows this launch holds
+                if (__any_sync(0xffffffffu, lane < n && (myc < p.kv_col_base || myc - p.kv_col_base >= p.kv_cols))) {
                     if (lane == 0) raise_error(err, F3S_ERR_BAD_FORMAT);
                     aborted = true;
                     break;
@@ -397,15 +407,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     const uint32_t s = slot_of(bsp, l);
                     const uint32_t par = par_of(l) ^ 1u;
                     const uint64_t pol = h == 1 ? pol_last : (h == 2 ? pol_first : pol_normal);
+                    const int kr = 16 * (c - p.kv_col_base);  // first row of the block in K / V
                     auto issue = [&]() {
                         stage_col[s] = c;
                         mbar_arrive_expect_tx(full(s), 2 * C::TILE);
                         const uint32_t dst = kv_s + s * 2 * C::TILE;
-                        tma_load_3d_hint(dst, &maps.ka, full(s), 0, z0, 16 * c, pol);
-                        tma_load_3d_hint(dst + C::TILE, &maps.va, full(s), 0, z0, 16 * c, pol);
+                        tma_load_3d_hint(dst, &maps.ka, full(s), 0, z0, kr, pol);
+                        tma_load_3d_hint(dst + C::TILE, &maps.va, full(s), 0, z0, kr, pol);
                         if constexpr (C::NBOX == 2) {
-                            tma_load_3d_hint(dst + C::HA * 2048, &maps.kb, full(s), 0, z0 + C::HA, 16 * c, pol);
-                            tma_load_3d_hint(dst + C::TILE + C::HA * 2048, &maps.vb, full(s), 0, z0 + C::HA, 16 * c,
+                            tma_load_3d_hint(dst + C::HA * 2048, &maps.kb, full(s), 0, z0 + C::HA, kr, pol);
+                            tma_load_3d_hint(dst + C::TILE + C::HA * 2048, &maps.vb, full(s), 0, z0 + C::HA, kr,
                                              pol);
                         }
                     };
@@ -923,39 +934,37 @@ static bool encode_map(CUtensorMap* m, const void* base, int rows, int heads, in
     return r == CUDA_SUCCESS;
 }
 
-// Per-device, per-variant "max dynamic shared memory" attribute.
+// Per-variant "max dynamic shared memory" attribute, set once per CUDA
+// context of each device (a device reset makes a new context that needs it
+// again); thread-safe.
 template <int D, int HG>
 static int ensure_smem_attr() {
-    static int done[64] = {};
-    int dev = 0;
-    F3S_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 64 && done[dev]) return F3S_SUCCESS;
-    F3S_CUDA_TRY(cudaFuncSetAttribute(k_fused3s<D, HG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      FwdCfg<D, HG>::SMEM));
-    if (dev < 64) done[dev] = 1;
-    return F3S_SUCCESS;
+    static PerContext<int> once;
+    return once.get(nullptr, [](int*) -> int {
+        F3S_CUDA_TRY(cudaFuncSetAttribute(k_fused3s<D, HG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          FwdCfg<D, HG>::SMEM));
+        return F3S_SUCCESS;
+    });
 }
 
 template <int D, int HG>
-static int launch_variant(const void* Q, const void* K, const void* V, FwdParams prm, int q_rows,
-                          cudaStream_t stream) {
+static int launch_variant(const void* Q, const void* K, const void* V, FwdParams prm, int q_rows, int kv_rows,
+                          bool merge, cudaStream_t stream) {
     using C = FwdCfg<D, HG>;
     int rc = ensure_smem_attr<D, HG>();
     if (rc != F3S_SUCCESS) return rc;
     FwdMaps maps;
     const int hb = C::HB ? C::HB : 1;  // box b is unused when HB == 0; encode a valid map anyway
     if (!encode_map(&maps.qa, Q, q_rows, prm.heads, D, C::HA) || !encode_map(&maps.qb, Q, q_rows, prm.heads, D, hb) ||
-        !encode_map(&maps.ka, K, prm.num_nodes, prm.heads, D, C::HA) ||
-        !encode_map(&maps.kb, K, prm.num_nodes, prm.heads, D, hb) ||
-        !encode_map(&maps.va, V, prm.num_nodes, prm.heads, D, C::HA) ||
-        !encode_map(&maps.vb, V, prm.num_nodes, prm.heads, D, hb))
+        !encode_map(&maps.ka, K, kv_rows, prm.heads, D, C::HA) || !encode_map(&maps.kb, K, kv_rows, prm.heads, D, hb) ||
+        !encode_map(&maps.va, V, kv_rows, prm.heads, D, C::HA) || !encode_map(&maps.vb, V, kv_rows, prm.heads, D, hb))
         return F3S_ERR_INVALID_VALUE;
     const int sms = num_sms_of_current_device();
     const int items = prm.num_items * prm.groups;
     const int grid = prm.plan ? sms : std::max(1, std::min(items, sms));
     k_fused3s<D, HG><<<grid, kFwdThreads, C::SMEM, stream>>>(maps, prm);
     F3S_LAUNCH_CHECK();
-    if (prm.plan) {
+    if (prm.plan && merge) {
         k_merge_pieces<D><<<2 * sms, 256, 0, stream>>>(prm.plan, prm.O, prm.heads, prm.num_nodes, prm.q_window_base,
                                                        prm.q_rows, prm.o_dtype);
         F3S_LAUNCH_CHECK();
@@ -996,9 +1005,80 @@ static LoadedPlanLayout loaded_plan_layout(int num_pieces, int num_split, int nu
     return L;
 }
 
-// Host-side validation keeps every index the kernels derive from the plan
-// inside its buffers: piece ranges inside their window's blocks, partial
-// slots below num_split_pieces, split records inside the slot range.
+// Host-side validation of a caller-built plan.  Every index the kernels
+// derive from it stays inside its buffers (piece ranges inside their
+// window's blocks, slots below num_split_pieces, split records inside the
+// slot range), and the plan is consistent, so the result is the same as the
+// unsplit forward:
+//   * the pieces of a window cover its blocks [offsets[w], offsets[w+1])
+//     exactly once; a piece holds at least one block, except the single
+//     piece of a window that has none;
+//   * a window of one piece has slot -1 and no split record;
+//   * a window of several pieces has one split record (w, first, count)
+//     with count equal to its pieces, and its pieces use the slots first ...
+//     first + count - 1, each exactly once;
+//   * no two split records share a slot.
+static int validate_plan(const int32_t* pieces, int num_pieces, const int32_t* splits, int num_split,
+                         int num_split_pieces, const int32_t* offsets, int nrw) {
+    for (int i = 0; i < num_pieces; ++i) {
+        const int32_t* pc = pieces + 4 * (size_t)i;
+        if (pc[0] < 0 || pc[0] >= nrw || pc[1] < offsets[pc[0]] || pc[2] < pc[1] || pc[2] > offsets[pc[0] + 1] ||
+            pc[3] < -1 || pc[3] >= num_split_pieces)
+            return F3S_ERR_BAD_FORMAT;
+    }
+    // split records: at most one per window, slot ranges disjoint
+    std::vector<int> split_of(nrw, -1);
+    std::vector<int> slot_owner(num_split_pieces, -1);
+    for (int i = 0; i < num_split; ++i) {
+        const int32_t* sw = splits + 4 * (size_t)i;
+        if (sw[0] < 0 || sw[0] >= nrw || sw[1] < 0 || sw[2] < 1 || (int64_t)sw[1] + sw[2] > num_split_pieces)
+            return F3S_ERR_BAD_FORMAT;
+        if (split_of[sw[0]] >= 0) return F3S_ERR_BAD_FORMAT;
+        split_of[sw[0]] = i;
+        for (int k = sw[1]; k < sw[1] + sw[2]; ++k) {
+            if (slot_owner[k] >= 0) return F3S_ERR_BAD_FORMAT;
+            slot_owner[k] = sw[0];
+        }
+    }
+    // pieces grouped by window: coverage and slot use
+    std::vector<int> idx(num_pieces);
+    for (int i = 0; i < num_pieces; ++i) idx[i] = i;
+    std::sort(idx.begin(), idx.end(), [&](int a, int b) {
+        const int32_t* pa = pieces + 4 * (size_t)a;
+        const int32_t* pb = pieces + 4 * (size_t)b;
+        return pa[0] != pb[0] ? pa[0] < pb[0] : pa[1] < pb[1];
+    });
+    std::vector<char> slot_used(num_split_pieces, 0);
+    for (int i = 0; i < num_pieces;) {
+        const int w = pieces[4 * (size_t)idx[i]];
+        int j = i;
+        while (j < num_pieces && pieces[4 * (size_t)idx[j]] == w) ++j;
+        const int n = j - i;
+        const int b0 = offsets[w], b1 = offsets[w + 1];
+        int at = b0;
+        for (int k = i; k < j; ++k) {
+            const int32_t* pc = pieces + 4 * (size_t)idx[k];
+            if (pc[1] != at) return F3S_ERR_BAD_FORMAT;  // gap or overlap
+            if (pc[2] == pc[1] && !(b1 == b0 && n == 1)) return F3S_ERR_BAD_FORMAT;
+            at = pc[2];
+            if (n == 1) {
+                if (pc[3] != -1 || split_of[w] >= 0) return F3S_ERR_BAD_FORMAT;
+            } else {
+                if (pc[3] < 0 || slot_owner[pc[3]] != w || slot_used[pc[3]]) return F3S_ERR_BAD_FORMAT;
+                slot_used[pc[3]] = 1;
+            }
+        }
+        if (at != b1) return F3S_ERR_BAD_FORMAT;
+        if (n > 1 && (split_of[w] < 0 || splits[4 * (size_t)split_of[w] + 2] != n)) return F3S_ERR_BAD_FORMAT;
+        i = j;
+    }
+    // every split record's window has its pieces
+    for (int i = 0; i < num_split; ++i)
+        for (int k = splits[4 * (size_t)i + 1]; k < splits[4 * (size_t)i + 1] + splits[4 * (size_t)i + 2]; ++k)
+            if (!slot_used[k]) return F3S_ERR_BAD_FORMAT;
+    return F3S_SUCCESS;
+}
+
 int load_plan_impl(const int32_t* pieces, int num_pieces, const int32_t* splits, int num_split,
                    int num_split_pieces, const int32_t* offsets, int nrw, int heads, int head_dim, void* plan,
                    size_t plan_bytes, cudaStream_t stream) {
@@ -1009,17 +1089,9 @@ int load_plan_impl(const int32_t* pieces, int num_pieces, const int32_t* splits,
     const LoadedPlanLayout L = loaded_plan_layout(num_pieces, num_split, num_split_pieces, heads, head_dim);
     if (plan_bytes < L.total) return F3S_ERR_WORKSPACE;
     if ((int64_t)num_pieces * L.groups > INT32_MAX) return F3S_ERR_TOO_LARGE;
-    for (int i = 0; i < num_pieces; ++i) {
-        const int32_t* pc = pieces + 4 * (size_t)i;
-        if (pc[0] < 0 || pc[0] >= nrw || pc[1] < offsets[pc[0]] || pc[2] < pc[1] || pc[2] > offsets[pc[0] + 1] ||
-            pc[3] < -1 || pc[3] >= num_split_pieces)
-            return F3S_ERR_BAD_FORMAT;
-    }
-    for (int i = 0; i < num_split; ++i) {
-        const int32_t* sw = splits + 4 * (size_t)i;
-        if (sw[0] < 0 || sw[0] >= nrw || sw[1] < 0 || sw[2] < 1 || (int64_t)sw[1] + sw[2] > num_split_pieces)
-            return F3S_ERR_BAD_FORMAT;
-    }
+    if (num_split > 0 && !offsets) return F3S_ERR_INVALID_VALUE;
+    const int rc = validate_plan(pieces, num_pieces, splits, num_split, num_split_pieces, offsets, nrw);
+    if (rc != F3S_SUCCESS) return rc;
     PlanHeader h{};
     h.num_pieces = h.max_pieces = num_pieces;
     h.num_split = h.max_split = num_split;
@@ -1084,7 +1156,7 @@ int make_plan_impl(const int* offsets, const int* order, int num_items, int64_t 
 int forward_impl(const void* Q, const void* K, const void* V, void* O, int o_dtype, const int* offsets,
                  const int* cols, const int* order, const uint8_t* block_hints, const void* plan, int num_items,
                  int num_nodes, int heads, int head_dim, int q_window_base, int q_rows, void* ws, size_t ws_bytes,
-                 cudaStream_t stream, uint64_t timeout_ns) {
+                 cudaStream_t stream, uint64_t timeout_ns, const PieceRange& range) {
     if (o_dtype != F3S_OUT_F32 && o_dtype != F3S_OUT_F16 && o_dtype != F3S_OUT_BF16) return F3S_ERR_INVALID_VALUE;
     if (num_items < 0 || num_nodes < 0 || heads <= 0 || q_window_base < 0 || q_rows < 0)
         return F3S_ERR_INVALID_VALUE;
@@ -1092,8 +1164,19 @@ int forward_impl(const void* Q, const void* K, const void* V, void* O, int o_dty
     if (!ws) return F3S_ERR_INVALID_VALUE;
     if (ws_bytes < kWsHeaderBytes) return F3S_ERR_WORKSPACE;
     if ((int64_t)heads * head_dim * 2 * 16 > (int64_t)1 << 40) return F3S_ERR_TOO_LARGE;
+    // the piece range and the K / V slice
+    if (!plan && (range.begin != 0 || range.end != -1)) return F3S_ERR_INVALID_VALUE;
+    if (range.begin < 0 || (range.end != -1 && range.end < range.begin)) return F3S_ERR_INVALID_VALUE;
+    const int kv_rows = range.kv_rows < 0 ? num_nodes : range.kv_rows;
+    if (range.kv_col_base < 0 || (int64_t)range.kv_col_base * 16 + kv_rows > (int64_t)num_nodes)
+        return F3S_ERR_INVALID_VALUE;
+    // a slice that stops inside the graph must end on a block-column boundary
+    if (kv_rows % 16 != 0 && (int64_t)range.kv_col_base * 16 + kv_rows != (int64_t)num_nodes)
+        return F3S_ERR_INVALID_VALUE;
     if (plan) num_items = 0;  // the plan lists the work
-    if ((!plan && num_items == 0) || num_nodes == 0 || q_rows == 0) return F3S_SUCCESS;
+    if ((!plan && num_items == 0) || num_nodes == 0 || q_rows == 0 || (plan && range.end == range.begin))
+        return F3S_SUCCESS;
+    if (kv_rows == 0) return F3S_ERR_INVALID_VALUE;
     if (!Q || !K || !V || !O || !offsets || !cols || (!plan && !order)) return F3S_ERR_INVALID_VALUE;
     auto misaligned = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) != 0; };
     if (misaligned(Q) || misaligned(K) || misaligned(V) || misaligned(O)) return F3S_ERR_INVALID_VALUE;
@@ -1117,23 +1200,48 @@ int forward_impl(const void* Q, const void* K, const void* V, void* O, int o_dty
     prm.q_windows = (int)(((int64_t)q_rows + 15) / 16);
     prm.q_rows = q_rows;
     prm.tail = num_nodes & 15;
+    prm.piece_begin = range.begin;
+    prm.piece_end = range.end;
+    prm.kv_col_base = range.kv_col_base;
+    prm.kv_cols = (int)(((int64_t)kv_rows + 15) / 16);
     if ((int64_t)num_items * prm.groups > INT32_MAX) return F3S_ERR_TOO_LARGE;
     // zero the abort flag and the ticket counter (adjacent words); the
     // status word stays sticky
     F3S_CUDA_TRY(cudaMemsetAsync(ws, 0, 2 * sizeof(int), stream));
+    const bool m = range.merge;
     if (head_dim == 64) {
         switch (hg) {
-            case 1: return launch_variant<64, 1>(Q, K, V, prm, q_rows, stream);
-            case 2: return launch_variant<64, 2>(Q, K, V, prm, q_rows, stream);
-            case 4: return launch_variant<64, 4>(Q, K, V, prm, q_rows, stream);
-            default: return launch_variant<64, 8>(Q, K, V, prm, q_rows, stream);
+            case 1: return launch_variant<64, 1>(Q, K, V, prm, q_rows, kv_rows, m, stream);
+            case 2: return launch_variant<64, 2>(Q, K, V, prm, q_rows, kv_rows, m, stream);
+            case 4: return launch_variant<64, 4>(Q, K, V, prm, q_rows, kv_rows, m, stream);
+            default: return launch_variant<64, 8>(Q, K, V, prm, q_rows, kv_rows, m, stream);
         }
     }
     switch (hg) {
-        case 1: return launch_variant<128, 1>(Q, K, V, prm, q_rows, stream);
-        case 2: return launch_variant<128, 2>(Q, K, V, prm, q_rows, stream);
-        default: return launch_variant<128, 4>(Q, K, V, prm, q_rows, stream);
+        case 1: return launch_variant<128, 1>(Q, K, V, prm, q_rows, kv_rows, m, stream);
+        case 2: return launch_variant<128, 2>(Q, K, V, prm, q_rows, kv_rows, m, stream);
+        default: return launch_variant<128, 4>(Q, K, V, prm, q_rows, kv_rows, m, stream);
     }
+}
+
+// The merge of a plan's split windows on its own (after f3s_forward_pieces
+// ran every piece of those windows).
+int plan_merge_impl(const void* plan, void* O, int o_dtype, int num_nodes, int heads, int head_dim,
+                    int q_window_base, int q_rows, cudaStream_t stream) {
+    if (o_dtype != F3S_OUT_F32 && o_dtype != F3S_OUT_F16 && o_dtype != F3S_OUT_BF16) return F3S_ERR_INVALID_VALUE;
+    if (num_nodes < 0 || heads <= 0 || q_window_base < 0 || q_rows < 0) return F3S_ERR_INVALID_VALUE;
+    if (head_dim != 64 && head_dim != 128) return F3S_ERR_UNSUPPORTED;
+    if (!plan || (reinterpret_cast<uintptr_t>(plan) & 255) != 0) return F3S_ERR_INVALID_VALUE;
+    if (num_nodes == 0 || q_rows == 0) return F3S_SUCCESS;
+    if (!O || (reinterpret_cast<uintptr_t>(O) & 15) != 0) return F3S_ERR_INVALID_VALUE;
+    const int sms = num_sms_of_current_device();
+    const PlanHeader* ph = static_cast<const PlanHeader*>(plan);
+    if (head_dim == 64)
+        k_merge_pieces<64><<<2 * sms, 256, 0, stream>>>(ph, O, heads, num_nodes, q_window_base, q_rows, o_dtype);
+    else
+        k_merge_pieces<128><<<2 * sms, 256, 0, stream>>>(ph, O, heads, num_nodes, q_window_base, q_rows, o_dtype);
+    F3S_LAUNCH_CHECK();
+    return F3S_SUCCESS;
 }
 
 // -------------------------------------------------- failure-path self-test --
@@ -1178,6 +1286,7 @@ size_t f3s_plan_size(int32_t num_items, int64_t num_blocks, int32_t max_blocks_p
 int f3s_make_plan(const int32_t* d_window_offsets, const int32_t* d_order, int32_t num_items, int64_t num_blocks,
                   int32_t max_blocks_per_piece, int32_t heads, int32_t head_dim, void* d_plan, size_t plan_bytes,
                   f3s_stream_t stream) {
+    f3s::NvtxRange nvtx_("f3s_make_plan");
     return f3s::make_plan_impl(d_window_offsets, d_order, num_items, num_blocks, max_blocks_per_piece, heads,
                                head_dim, d_plan, plan_bytes, (cudaStream_t)stream);
 }
@@ -1200,9 +1309,35 @@ int f3s_forward(const void* d_Q, const void* d_K, const void* d_V, float* d_O, c
                 const int32_t* d_block_cols, const int32_t* d_order, const uint8_t* d_block_hints, const void* d_plan,
                 int32_t num_items, int32_t num_nodes, int32_t heads, int32_t head_dim, int32_t q_window_base,
                 int32_t q_rows, void* d_workspace, size_t workspace_bytes, f3s_stream_t stream) {
+    f3s::NvtxRange nvtx_("f3s_forward");
     return f3s::forward_impl(d_Q, d_K, d_V, d_O, F3S_OUT_F32, d_window_offsets, d_block_cols, d_order,
                              d_block_hints, d_plan, num_items, num_nodes, heads, head_dim, q_window_base, q_rows,
-                             d_workspace, workspace_bytes, (cudaStream_t)stream, f3s::kWaitTimeoutNs);
+                             d_workspace, workspace_bytes, (cudaStream_t)stream, f3s::kWaitTimeoutNs, f3s::PieceRange{});
+}
+
+int f3s_forward_pieces(const void* d_Q, const void* d_K, const void* d_V, void* d_O, int32_t o_dtype,
+                       const int32_t* d_window_offsets, const int32_t* d_block_cols, const uint8_t* d_block_hints,
+                       const void* d_plan, int32_t piece_begin, int32_t piece_end, int32_t kv_col_base,
+                       int32_t kv_rows, int32_t num_nodes, int32_t heads, int32_t head_dim, int32_t q_window_base,
+                       int32_t q_rows, void* d_workspace, size_t workspace_bytes, f3s_stream_t stream) {
+    f3s::NvtxRange nvtx_("f3s_forward_pieces");
+    if (!d_plan || kv_rows < 0) return F3S_ERR_INVALID_VALUE;
+    f3s::PieceRange r;
+    r.begin = piece_begin;
+    r.end = piece_end;
+    r.kv_col_base = kv_col_base;
+    r.kv_rows = kv_rows;
+    r.merge = false;
+    return f3s::forward_impl(d_Q, d_K, d_V, d_O, o_dtype, d_window_offsets, d_block_cols, nullptr, d_block_hints,
+                             d_plan, 0, num_nodes, heads, head_dim, q_window_base, q_rows, d_workspace,
+                             workspace_bytes, (cudaStream_t)stream, f3s::kWaitTimeoutNs, r);
+}
+
+int f3s_plan_merge(const void* d_plan, void* d_O, int32_t o_dtype, int32_t num_nodes, int32_t heads,
+                   int32_t head_dim, int32_t q_window_base, int32_t q_rows, f3s_stream_t stream) {
+    f3s::NvtxRange nvtx_("f3s_plan_merge");
+    return f3s::plan_merge_impl(d_plan, d_O, o_dtype, num_nodes, heads, head_dim, q_window_base, q_rows,
+                                (cudaStream_t)stream);
 }
 
 int f3s_forward_ex(const void* d_Q, const void* d_K, const void* d_V, void* d_O, int32_t o_dtype,
@@ -1210,9 +1345,10 @@ int f3s_forward_ex(const void* d_Q, const void* d_K, const void* d_V, void* d_O,
                    const uint8_t* d_block_hints, const void* d_plan, int32_t num_items, int32_t num_nodes,
                    int32_t heads, int32_t head_dim, int32_t q_window_base, int32_t q_rows, void* d_workspace,
                    size_t workspace_bytes, f3s_stream_t stream) {
+    f3s::NvtxRange nvtx_("f3s_forward");
     return f3s::forward_impl(d_Q, d_K, d_V, d_O, o_dtype, d_window_offsets, d_block_cols, d_order, d_block_hints,
                              d_plan, num_items, num_nodes, heads, head_dim, q_window_base, q_rows, d_workspace,
-                             workspace_bytes, (cudaStream_t)stream, f3s::kWaitTimeoutNs);
+                             workspace_bytes, (cudaStream_t)stream, f3s::kWaitTimeoutNs, f3s::PieceRange{});
 }
 
 int f3s_selftest_wait_timeout(uint64_t timeout_ns, void* d_workspace, size_t workspace_bytes, f3s_stream_t stream) {

@@ -3,7 +3,9 @@
 // scan primitives.
 #pragma once
 #include <cstdint>
+#include <mutex>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 #include "fused3s.h"
 #include "f3s_ptx.cuh"
 
@@ -30,6 +32,56 @@ inline ErrorSink sink_of(void* ws) {
 // Host-side: remember the CUDA error behind an F3S_ERR_CUDA return.
 void note_cuda_error(cudaError_t e);
 
+// ------------------------------------------------------ per-context state --
+// The calling thread's current CUDA context: its device and the driver's
+// unique context id (cuCtxGetId).  Host-side state the library keeps per
+// device -- kernel attributes, the no-alloc scratch address, library-owned
+// workspaces -- belongs to one context: cudaDeviceReset destroys it and the
+// next primary context of the device gets a new id, so every such cache is
+// keyed on the id and rebuilt when it changes.
+constexpr int kMaxDevices = 64;
+struct ContextKey {
+    int device;
+    unsigned long long id;
+};
+int current_context(ContextKey* key);
+
+// A value computed once per context of each device, under a lock (several
+// host threads may call the library at once).  get() returns the cached
+// value when it was made in the current context, else calls make(&value)
+// and caches it on success.
+template <class T>
+class PerContext {
+  public:
+    template <class Make>
+    int get(T* out, Make&& make) {
+        ContextKey k{};
+        int rc = current_context(&k);
+        if (rc != F3S_SUCCESS) return rc;
+        std::lock_guard<std::mutex> lock(mu_);
+        Slot& s = slots_[k.device];
+        if (!s.valid || s.id != k.id) {
+            T v{};
+            rc = make(&v);
+            if (rc != F3S_SUCCESS) return rc;
+            s.value = v;
+            s.id = k.id;
+            s.valid = true;
+        }
+        if (out) *out = s.value;
+        return F3S_SUCCESS;
+    }
+
+  private:
+    struct Slot {
+        bool valid = false;
+        unsigned long long id = 0;
+        T value{};
+    };
+    std::mutex mu_;
+    Slot slots_[kMaxDevices];
+};
+
 #define F3S_CUDA_TRY(call)                       \
     do {                                         \
         cudaError_t e_ = (call);                 \
@@ -49,6 +101,33 @@ void note_cuda_error(cudaError_t e);
     } while (0)
 
 int num_sms_of_current_device();
+
+// NVTX range around an entry point's host side (its enqueue), named after
+// the call; free when no profiler is attached.
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
+
+// The part of a plan one forward launch runs, and the K / V rows it holds:
+// pieces [begin, end) of the plan (end -1: to the last), K / V holding the
+// graph's rows 16 * kv_col_base ... 16 * kv_col_base + kv_rows - 1 (kv_rows -1:
+// all rows from 0), and whether the split windows are merged right after.
+struct PieceRange {
+    int begin = 0;
+    int end = -1;
+    int kv_col_base = 0;
+    int kv_rows = -1;
+    bool merge = true;
+};
+
+// The fused forward behind every forward entry point (f3s_forward.cu).
+int forward_impl(const void* Q, const void* K, const void* V, void* O, int o_dtype, const int* offsets,
+                 const int* cols, const int* order, const uint8_t* block_hints, const void* plan, int num_items,
+                 int num_nodes, int heads, int head_dim, int q_window_base, int q_rows, void* ws, size_t ws_bytes,
+                 cudaStream_t stream, uint64_t timeout_ns, const PieceRange& range);
 
 // ------------------------------------------------------------------ scans --
 __device__ __forceinline__ int warp_inclusive_scan(int v) {

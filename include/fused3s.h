@@ -223,15 +223,52 @@ int f3s_make_plan(const int32_t* d_window_offsets, const int32_t* d_order, int32
  *   (window, first slot, pieces, 0): its pieces own slots first ...
  *   first + pieces - 1 and are merged in slot order (deterministic).
  * h_window_offsets: the format's offsets on the host (validation only).
- * Copies synchronously; every index is validated (F3S_ERR_BAD_FORMAT).
+ * Copies synchronously.  The plan is validated on the host and rejected
+ * with F3S_ERR_BAD_FORMAT unless: every index lies in range; the pieces of
+ * each listed window cover its blocks exactly once (no gap, no overlap),
+ * each holding at least one block except the single piece of a window
+ * without blocks; a window of one piece has slot -1 and no split record; a
+ * window of several pieces has exactly one split record whose count equals
+ * its pieces, and its pieces use that record's slots, each exactly once; no
+ * two split records share a slot.
  * The plan then serves f3s_forward / f3s_forward_ex like one from
- * f3s_make_plan (d_order / num_items unused).
+ * f3s_make_plan (d_order / num_items unused), and f3s_forward_pieces.
  * ---------------------------------------------------------------------- */
 size_t f3s_plan_size_for(int32_t num_pieces, int32_t num_split, int32_t num_split_pieces, int32_t heads,
                          int32_t head_dim);
 int f3s_load_plan(const int32_t* h_pieces, int32_t num_pieces, const int32_t* h_splits, int32_t num_split,
                   int32_t num_split_pieces, const int32_t* h_window_offsets, int32_t num_row_windows, int32_t heads,
                   int32_t head_dim, void* d_plan, size_t plan_bytes, f3s_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Part of a plan's work, with K / V holding only some block columns (no
+ * reference counterpart: the reference reads all of K / V on one device).
+ *
+ * Runs pieces [piece_begin, piece_end) of d_plan (piece_end -1: to the
+ * plan's last piece) and does not merge.  d_K / d_V hold the graph's rows
+ * 16 * kv_col_base ... 16 * kv_col_base + kv_rows - 1 (kv_rows ends on a
+ * block-column boundary unless it reaches num_nodes); every block of the
+ * launched pieces must have its column inside that range
+ * (F3S_ERR_BAD_FORMAT otherwise, through f3s_workspace_status).  A piece of
+ * a window of one piece (slot -1) writes the window's O rows; a piece of a
+ * split window writes its partial softmax state into the plan.  Once every
+ * piece of the split windows has run -- over one or several calls, e.g. one
+ * per K / V slice passed around a ring of GPUs -- f3s_plan_merge writes
+ * their O rows.  f3s_forward_ex with a plan equals f3s_forward_pieces over
+ * all pieces with the whole K / V, then f3s_plan_merge.
+ * Other arguments as f3s_forward_ex (d_order is not needed).
+ * ---------------------------------------------------------------------- */
+int f3s_forward_pieces(const void* d_Q, const void* d_K, const void* d_V, void* d_O, int32_t o_dtype,
+                       const int32_t* d_window_offsets, const int32_t* d_block_cols, const uint8_t* d_block_hints,
+                       const void* d_plan, int32_t piece_begin, int32_t piece_end, int32_t kv_col_base,
+                       int32_t kv_rows, int32_t num_nodes, int32_t heads, int32_t head_dim, int32_t q_window_base,
+                       int32_t q_rows, void* d_workspace, size_t workspace_bytes, f3s_stream_t stream);
+
+/* Combines the partial states of every split window of d_plan (in slot
+ * order: deterministic) and writes their O rows ([q_rows, heads, head_dim]
+ * of o_dtype, rows 16 * q_window_base ...). */
+int f3s_plan_merge(const void* d_plan, void* d_O, int32_t o_dtype, int32_t num_nodes, int32_t heads,
+                   int32_t head_dim, int32_t q_window_base, int32_t q_rows, f3s_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * L2 eviction hints for f3s_forward, one per active block (no reference
@@ -258,7 +295,11 @@ int f3s_block_hints(const int32_t* d_window_offsets, const int32_t* d_block_cols
  * feat_dim columns, one head, and every one of those rows is treated as a
  * real node (the reference v2 kernel cannot know N, so padded columns are
  * not masked -- call f3s_forward with the true num_nodes for masking).
- * Uses a library-owned per-device workspace (allocated on first use).
+ * Uses a library-owned workspace (the launch's work counter and status
+ * word) per CUDA context and stream, allocated (256 bytes) on the first
+ * launch on that stream and kept until the process exits: launches on
+ * different streams may run concurrently; launches on one stream run in
+ * stream order.
  * ---------------------------------------------------------------------- */
 int f3s_1tb1rw_launch(const void* Q, const void* K, const void* V, float* O_out,
                       const int32_t* window_offsets, const int32_t* block_col_indices,

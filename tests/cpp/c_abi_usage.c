@@ -1,5 +1,5 @@
-/* The C-ABI call sequence a C caller of fused3S would write (the same calls
- * as INTEGRATION.md shows), compiled with a C compiler to keep the header
+/* The C-ABI call sequence a C caller of fused3S would write (convert, order,
+ * plan, hints, forward, status), compiled with a C compiler to keep the header
  * plain C.  Not executed: it only has to compile against include/fused3s.h. */
 #include <stdint.h>
 #include <stdlib.h>

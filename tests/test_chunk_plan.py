@@ -35,15 +35,16 @@ def _loop(off, cols, order, cw, T):
             slot += len(ps)
         else:
             slots.append([-1] * len(ps))
-    chunks = sorted({c for ps in items for c, _, _ in ps})
+    chunks = sorted({c for ps in items for c, _, _ in ps} | {0})
     for c in chunks:
         for i, (w, ps) in enumerate(zip(order, items)):
             for k, (cc, lo, hi) in enumerate(ps):
                 if cc == c:
                     pieces.append((w, lo, hi, slots[i][k]))
-    for w, ps in zip(order, items):
-        if not ps:
-            pieces.append((w, off[w], off[w], -1))
+        if c == 0:  # windows without blocks: one empty piece each, with chunk 0
+            for w, ps in zip(order, items):
+                if not ps:
+                    pieces.append((w, off[w], off[w], -1))
     return np.array(pieces, np.int32).reshape(-1, 4), np.array(splits, np.int32).reshape(-1, 4), slot
 
 
@@ -65,8 +66,14 @@ def test_chunk_pieces_invariants_with_empty_windows_and_subsets():
     g = G.csr_from_edges(n, src, rng.integers(0, n, 20000))
     off, cols = oracle.convert(n, g.row_ptr, g.col_ind)
     order = oracle.window_order(off)[::2]  # a subset of the windows
-    pieces, splits, n_slots = column_chunk_pieces(off, cols, order, 16, 5)
+    pieces, splits, n_slots, starts = column_chunk_pieces(off, cols, order, 16, 5)
     cw = 16
+    # the chunk ranges partition the pieces, each range one column chunk
+    assert starts[0] == 0 and starts[-1] == pieces.shape[0]
+    for c in range(starts.shape[0] - 1):
+        for w, lo, hi, s in pieces[starts[c]:starts[c + 1]]:
+            if hi > lo:
+                assert cols[lo] // cw == c
     covered = {}
     for w, lo, hi, s in pieces:
         assert off[w] <= lo <= hi <= off[w + 1]
@@ -84,3 +91,26 @@ def test_chunk_pieces_invariants_with_empty_windows_and_subsets():
     for w, first, cnt, _ in splits:
         mine = sorted((lo, s) for ww, lo, hi, s in pieces if ww == w)
         assert [s for _, s in mine] == list(range(first, first + cnt))
+
+
+def test_explicit_cuts_equal_multiples_and_cover_uneven_slices():
+    g = G.powerlaw_graph(num_nodes=1203, directed_edges=9000, max_degree=300, seed=11)
+    off, cols = oracle.convert(g.num_nodes, g.row_ptr, g.col_ind)
+    order = oracle.window_order(off)
+    nrw = off.shape[0] - 1
+    a = column_chunk_pieces(off, cols, order, 8, 0)
+    b = column_chunk_pieces(off, cols, order, col_cuts=np.arange(0, nrw + 8, 8))
+    for x, y in zip(a[:2], b[:2]):
+        assert np.array_equal(x, y)
+    assert a[2] == b[2]
+    # uneven slices (the K / V slices of a ring of 3 GPUs)
+    cuts = np.array([0, nrw // 3, (2 * nrw) // 3, nrw])
+    pieces, splits, n_slots, starts = column_chunk_pieces(off, cols, order, col_cuts=cuts)
+    for j in range(3):
+        for w, lo, hi, s in pieces[starts[j]:starts[j + 1]]:
+            if hi > lo:
+                assert cuts[j] <= cols[lo] and cols[hi - 1] < cuts[j + 1]
+    blocks = sorted(b for w, lo, hi, s in pieces for b in range(lo, hi))
+    assert blocks == list(range(off[-1]))
+    with pytest.raises(ValueError):
+        column_chunk_pieces(off, cols, order, col_cuts=np.array([0, nrw // 2]))  # does not cover

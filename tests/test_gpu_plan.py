@@ -186,7 +186,7 @@ def test_load_plan_rejects_out_of_range_pieces(lib):
     g = G.make_graph("c1")
     fmt = F.convert_csr_to_block_sparse(g.num_nodes, g.row_ptr, g.col_ind)
     off, cols = fmt.to_host()
-    pieces, splits, n_slots = F.column_chunk_pieces(off, cols, np.arange(fmt.num_row_windows), 8, 0)
+    pieces, splits, n_slots, _ = F.column_chunk_pieces(off, cols, np.arange(fmt.num_row_windows), 8, 0)
     size = lib.f3s_plan_size_for(pieces.shape[0], splits.shape[0], n_slots, 1, 64)
     buf = torch.empty(size, dtype=torch.uint8, device="cuda")
     off32 = np.ascontiguousarray(off.astype(np.int32))

@@ -36,8 +36,20 @@ def test_op_matches_fused3s_forward(lib):
     assert torch.equal(got, ref)
     plan = F.make_plan(fmt, 2, 64, order=order, max_blocks=6)
     ref_p = F.fused3s_forward(q, k, v, fmt, plan=plan, out_dtype=torch.float16)
-    got_p = op(q, k, v, fmt.window_offsets, fmt.block_col_indices, order, g.num_nodes, 0, torch.float16, None,
-               plan.buffer, plan.max_blocks)
+    opp = torch.ops.fused3s.block_attention_planned
+    got_p = opp(q, k, v, fmt.window_offsets, fmt.block_col_indices, g.num_nodes, plan.buffer, plan.max_blocks, 0,
+                torch.float16)
     assert torch.equal(got_p, ref_p)
     torch.library.opcheck(op, (q, k, v, fmt.window_offsets, fmt.block_col_indices, order, g.num_nodes),
                           test_utils=("test_schema", "test_faketensor"))
+    # the plan buffer is declared mutated (its partial states are written)
+    torch.library.opcheck(opp, (q, k, v, fmt.window_offsets, fmt.block_col_indices, g.num_nodes, plan.buffer,
+                                plan.max_blocks), test_utils=("test_schema", "test_faketensor"))
+
+
+def test_ops_declare_what_they_mutate():
+    def mutated(op):
+        return [a.name for a in op.default._schema.arguments if a.alias_info is not None and a.alias_info.is_write]
+
+    assert mutated(torch.ops.fused3s.block_attention) == []
+    assert mutated(torch.ops.fused3s.block_attention_planned) == ["plan"]
