@@ -171,6 +171,8 @@ def parse_int32_text(text, max_count: Optional[int] = None, device=None) -> torc
         text = np.frombuffer(bytes(text), dtype=np.uint8)
     if isinstance(text, np.ndarray):
         host = text.view(np.uint8).reshape(-1)
+        if not host.flags.writeable:  # e.g. a view of bytes; torch wants writable memory
+            host = host.copy()
         dev_text = torch.from_numpy(host).to(device)
     else:
         dev_text = text.to(device=device, dtype=torch.uint8).contiguous().view(-1)
@@ -310,14 +312,25 @@ class ForwardPlan:
     piece_ranges: Optional[list] = None
 
 
+# Longest run of blocks one work item accumulates.  The tensor cores add each
+# block's P.V into the fp32 O accumulator with truncation (round toward
+# zero), so an accumulator fed n blocks in a row drifts toward zero by about
+# n * 2^-26 of its value; hub windows of hundreds of thousands of blocks
+# would lose ~0.4 % (measured on C5).  Pieces of at most this many blocks are
+# merged with round-to-nearest fp32 arithmetic (k_merge_pieces), which keeps
+# the drift near 1e-4.
+MAX_PIECE_BLOCKS = 4096
+
+
 def auto_piece_blocks(num_blocks: int, device=None) -> int:
     """Piece size: a quarter of one SM's share of the blocks, so no single
-    window can hold one SM much past the others; never below 16 blocks (a
+    window can hold one SM much past the others, at most MAX_PIECE_BLOCKS
+    (accumulation accuracy of hub windows) and never below 16 blocks (a
     piece's partial state is about one block's K/V bytes, so a piece of 16
     blocks moves at most ~6 % more)."""
     device = _default_device(device)
     sms = torch.cuda.get_device_properties(device).multi_processor_count
-    return max(16, -(-int(num_blocks) // (4 * sms)))
+    return max(16, min(MAX_PIECE_BLOCKS, -(-int(num_blocks) // (4 * sms))))
 
 
 def make_plan(fmt: BlockSparseFormat, heads: int, head_dim: int, order: Optional[torch.Tensor] = None,

@@ -274,6 +274,34 @@ def make_features(num_nodes: int, heads: int, head_dim: int, kind: str = "unifor
     return tuple(out)
 
 
+def make_features_device(num_nodes: int, heads: int, head_dim: int, kind: str = "normal", seed: int = 42,
+                         device="cuda"):
+    """fp16 [num_nodes, heads, head_dim] Q, K, V drawn on the device in row
+    chunks (no fp32 copy of a whole tensor), for the large configurations.
+    Same distributions as make_features; the values depend on the chunking,
+    so they differ from make_features' for the same seed."""
+    if torch is None:
+        raise RuntimeError("make_features_device needs torch")
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    out = []
+    chunk = max(1, (1 << 27) // (heads * head_dim))
+    for _ in range(3):
+        t = torch.empty((num_nodes, heads, head_dim), dtype=torch.float16, device=dev)
+        for r in range(0, num_nodes, chunk):
+            rr = min(num_nodes, r + chunk)
+            if kind == "uniform":
+                x = torch.rand((rr - r, heads, head_dim), generator=gen, device=dev) * 2 - 1
+            elif kind == "normal":
+                x = torch.randn((rr - r, heads, head_dim), generator=gen, device=dev) / math.sqrt(head_dim)
+            else:
+                raise ValueError(kind)
+            t[r:rr] = x.to(torch.float16)
+        out.append(t)
+    return tuple(out)
+
+
 def graph_stats(g: CSRGraph) -> dict:
     deg = np.diff(g.row_ptr.astype(np.int64))
     return {

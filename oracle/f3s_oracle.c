@@ -10,6 +10,7 @@
  * fatalhawk/fused3S project root):
  *
  *   orc_convert            src/converter.cu:13-44
+ *   orc_convert_mt         the same, windows split over threads
  *   orc_window_order       include/utils.cuh:48-59 (stable tie order, see below)
  *   orc_block_attention    tests/test_fused_3s_v2.cu:17-59
  *   orc_edge_attention     baselines/cpu_baseline.cpp:16-91
@@ -77,6 +78,94 @@ int64_t orc_convert(int32_t num_nodes, const int32_t* row_ptr,
         offsets_out[w + 1] = (int32_t)total;
     }
     free(buf);
+    return total;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Threaded driver for orc_convert (large graphs)                           */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Same output as orc_convert.  Windows are cut into nthreads contiguous
+ * ranges; each worker runs orc_convert's per-window loop (the same
+ * statements, on the rows of its range) into its own buffer, and the
+ * buffers are concatenated in window order after the offsets are summed.
+ */
+typedef struct {
+    int32_t num_nodes;
+    const int32_t *row_ptr, *col_ind;
+    int32_t w0, w1;
+    int32_t* counts; /* [w1 - w0] unique block columns per window */
+    int32_t* cols;   /* the range's block columns, window after window */
+    int64_t ncols;
+} orc_conv_part;
+
+static void* orc_conv_worker(void* arg) {
+    orc_conv_part* p = (orc_conv_part*)arg;
+    int64_t cap = 0, total = 0, room = 0;
+    int32_t* buf = NULL;
+    for (int32_t w = p->w0; w < p->w1; ++w) {
+        int32_t start = w * 16;
+        int32_t end = start + 16 < p->num_nodes ? start + 16 : p->num_nodes;
+        int64_t len = 0;
+        for (int32_t u = start; u < end; ++u)
+            if (p->row_ptr[u + 1] > p->row_ptr[u]) len += p->row_ptr[u + 1] - p->row_ptr[u];
+        if (len > cap) {
+            cap = len * 2;
+            buf = (int32_t*)realloc(buf, (size_t)cap * sizeof(int32_t));
+        }
+        if (total + len > room) {
+            room = (total + len) * 2 + 1024;
+            p->cols = (int32_t*)realloc(p->cols, (size_t)room * sizeof(int32_t));
+        }
+        int64_t n = 0;
+        for (int32_t u = start; u < end; ++u)
+            for (int32_t j = p->row_ptr[u]; j < p->row_ptr[u + 1]; ++j)
+                buf[n++] = p->col_ind[j] / 16;
+        if (n > 1) qsort(buf, (size_t)n, sizeof(int32_t), cmp_i32);
+        int64_t before = total;
+        for (int64_t i = 0; i < n; ++i)
+            if (i == 0 || buf[i] != buf[i - 1]) p->cols[total++] = buf[i];
+        p->counts[w - p->w0] = (int32_t)(total - before);
+    }
+    free(buf);
+    p->ncols = total;
+    return NULL;
+}
+
+int64_t orc_convert_mt(int32_t num_nodes, const int32_t* row_ptr,
+                       const int32_t* col_ind, int32_t* offsets_out,
+                       int32_t* cols_out, int32_t nthreads) {
+    int32_t nrw = (num_nodes + 15) / 16;
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > nrw) nthreads = nrw > 0 ? nrw : 1;
+    orc_conv_part* parts = (orc_conv_part*)calloc((size_t)nthreads, sizeof(orc_conv_part));
+    pthread_t* th = (pthread_t*)calloc((size_t)nthreads, sizeof(pthread_t));
+    for (int32_t t = 0; t < nthreads; ++t) {
+        orc_conv_part* p = &parts[t];
+        p->num_nodes = num_nodes;
+        p->row_ptr = row_ptr;
+        p->col_ind = col_ind;
+        p->w0 = (int32_t)((int64_t)nrw * t / nthreads);
+        p->w1 = (int32_t)((int64_t)nrw * (t + 1) / nthreads);
+        p->counts = (int32_t*)malloc(((size_t)(p->w1 - p->w0) + 1) * sizeof(int32_t));
+        pthread_create(&th[t], NULL, orc_conv_worker, p);
+    }
+    int64_t total = 0;
+    offsets_out[0] = 0;
+    for (int32_t t = 0; t < nthreads; ++t) {
+        orc_conv_part* p = &parts[t];
+        pthread_join(th[t], NULL);
+        for (int32_t w = p->w0; w < p->w1; ++w) {
+            total += p->counts[w - p->w0];
+            offsets_out[w + 1] = (int32_t)total;
+        }
+        if (p->ncols) memcpy(cols_out + (total - p->ncols), p->cols, (size_t)p->ncols * sizeof(int32_t));
+        free(p->counts);
+        free(p->cols);
+    }
+    free(parts);
+    free(th);
     return total;
 }
 

@@ -141,3 +141,37 @@ def test_reference_loader_bug_is_fixed():
         pytest.skip("reference data not present")
     g = load_csr_graph(str(path))
     assert np.count_nonzero(g.col_ind) > 0.9 * g.num_edges
+
+
+def test_threaded_converter_equals_the_port():
+    g = G.rmat_graph(14, 16, device="cpu", name="small-rmat")
+    a = oracle.convert(g.num_nodes, g.row_ptr, g.col_ind)
+    for t in (2, 7, 64):
+        b = oracle.convert(g.num_nodes, g.row_ptr, g.col_ind, threads=t)
+        assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+
+
+@pytest.mark.parametrize("n", [16 * 97, 16 * 97 + 5])
+def test_compact_windows_is_bit_identical_to_the_full_problem(n):
+    """The sampled-window sub-problem used for large-graph parity (only the
+    sampled windows and the K/V blocks they use) gives the same bits as the
+    full problem, including the masked tail of the last block column."""
+    rng = np.random.default_rng(n)
+    src = rng.integers(0, n, 6000)
+    dst = rng.integers(0, n, 6000)
+    dst[:40] = n - 1  # the last (partial) block column is used
+    src[40:60] = n - 1  # and the last window has rows
+    g = G.csr_from_edges(n, src, dst)
+    off, cols = oracle.convert(n, g.row_ptr, g.col_ind)
+    H, d = 2, 64
+    q, k, v = (x.float().numpy() for x in G.make_features(n, H, d, kind="uniform", seed=3))
+    full = oracle.block_attention(n, q, k, v, off, cols)
+    nrw = off.shape[0] - 1
+    for wins in (np.array([3, 17, nrw - 1]), np.array([0, 5, 9, 44]), rng.choice(nrw, 20, replace=False)):
+        c = oracle.compact_windows(n, off, cols, wins)
+        qc, kc, vc = (oracle.gather_rows(x, r) for x, r in ((q, c["q_rows"]), (k, c["kv_rows"]), (v, c["kv_rows"])))
+        oc = oracle.block_attention(c["num_nodes"], qc, kc, vc, c["offsets"], c["cols"], windows=c["windows"])
+        for w, wc in zip(wins, c["windows"]):
+            rows = np.arange(16 * w, min(16 * w + 16, n))
+            crows = 16 * int(wc) + np.arange(rows.shape[0])
+            assert np.array_equal(oc[crows], full[rows]), w

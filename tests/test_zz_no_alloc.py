@@ -4,7 +4,8 @@ memory, or a service that never calls cudaMalloc / cudaFree after start-up).
 Its scratch is a fixed 32 MiB array inside the library.
 
 Called through the C ABI and checked against the existing entry point
-(f3s_convert, through the Python API) -- integer output, so bit for bit --
+(f3s_convert, through the Python API) and against the oracle's restatement
+of the reference converter -- integer output, so bit for bit --
 on two calls in a row, the second on a smaller graph so that anything the
 first call left in the shared array would show.  This file is collected
 last so that a run stopping at the first failure has run every other test.
@@ -16,6 +17,7 @@ import pytest
 import torch
 
 import fused3s_b200 as F
+import oracle
 from fused3s_b200 import _lib
 from fused3s_b200 import graphs as G
 
@@ -59,6 +61,10 @@ def test_noalloc_convert_matches_f3s_convert_twice(lib):
         want_off, want_cols = want.to_host()
         assert np.array_equal(off, want_off)
         assert np.array_equal(cols, want_cols)
+        # and the reference's converter, restated (bit for bit)
+        ref_off, ref_cols = oracle.convert(n, rp, ci)
+        assert np.array_equal(off, ref_off)
+        assert np.array_equal(cols, ref_cols)
 
 
 def test_noalloc_convert_limits_and_errors(lib):
