@@ -86,6 +86,12 @@ def measured_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def lib_is_default() -> bool:
+    """The library in use is the package's own build (not a FUSED3S_LIB override)."""
+    from fused3s_b200 import _lib
+    return Path(_lib.LIB_PATH).resolve() == (ROOT / "fused3s_b200" / "libfused3s.so").resolve()
+
+
 def ncu_traffic(config: str, heads: int, dim: int, split: str):
     """DRAM bytes (read + write) per fused-kernel launch of this exact
     workload, from the committed ncu summary (a one-pass capture of the
@@ -387,7 +393,7 @@ def run_ours(args):
     if args.l2_hints == "on":
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        hints = F.block_hints(fmt, H, d, order=my_order)
+        hints = F.block_hints(fmt, H, d, order=my_order, l2_fraction=args.l2_keep)
         torch.cuda.synchronize()
         hints_ms = (time.perf_counter() - t0) * 1e3
     hints_ptr = hints.data_ptr() if hints is not None else None
@@ -638,7 +644,8 @@ def run_ours(args):
     hbm_peak, tc_peak, peak_kind = measured_peaks()
     achieved = bytes_launch / (kernel_ms / 1e3) / 1e9
     traffic = ncu_traffic(args.config, H, d, args.split) if (world == 1 and args.graph_seed is None
-                                                             and args.l2_hints == "on") else None
+                                                             and args.l2_hints == "on" and args.l2_keep == 0.5
+                                                             and lib_is_default()) else None
 
     result = None
     if rank == 0:
@@ -667,7 +674,7 @@ def run_ours(args):
                        "l2": "inputs larger than L2" if (Kf.numel() + Vf.numel()) * 2 > 126e6 else
                              "inputs fit in L2 (no flush)",
                        "convert_ms": convert_ms, "order_ms": order_ms, "l2_hints": args.l2_hints,
-                       "cuda_graph": args.graph, "o_dtype": args.out_dtype,
+                       "cuda_graph": args.graph, "o_dtype": args.out_dtype, "l2_keep": args.l2_keep,
                        "precision": "f16 Q/K/V and P on the tensor cores, f32 accumulation and softmax state",
                        "hints_ms": hints_ms, "split": args.split,
                        "piece_blocks": plan.max_blocks if plan is not None else None, "plan_ms": plan_ms},
@@ -716,6 +723,8 @@ def main(argv=None):
                          "chunked[:block columns] (pieces cut at column-chunk boundaries, swept chunk by chunk)")
     ap.add_argument("--l2-hints", default="on", choices=["on", "off"],
                     help="per block L2 eviction hints (computed once per graph)")
+    ap.add_argument("--l2-keep", type=float, default=0.5,
+                    help="fraction of the L2 given to the most popular block columns (evict-last hints)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU work for cpu_baseline")

@@ -82,6 +82,18 @@ struct FwdCfg {
     static constexpr int S_SUB = (STAGES_FIT > 32 ? 32 : STAGES_FIT) / SPLITS;
     static constexpr int STAGES = S_SUB * SPLITS;
     static_assert(S_SUB >= 2, "need at least two stages per split");
+    // Blocks a consumer warp takes per step (one max update and one vote per
+    // step; their QK^T / exp / P.V chains interleave).  A step holds NB
+    // stages of the split's sub-ring until its end, so NB leaves stages for
+    // the producer to keep loading (d = 128: one block, its O accumulator
+    // is 64 registers).
+#ifndef F3S_BLOCKS_PER_STEP
+#define F3S_BLOCKS_PER_STEP 3
+#endif
+    static constexpr int NB_WANT = D == 64 ? F3S_BLOCKS_PER_STEP : 2;
+    static constexpr int NB_ROOM = S_SUB - 2 > 1 ? S_SUB - 2 : 1;  // keep two stages loading if possible
+    static constexpr int NB = NB_WANT < NB_ROOM ? NB_WANT : NB_ROOM;
+    static_assert(NB >= 1 && NB < S_SUB, "a step must leave the producer a stage");
     // blocks the producer issues per round (one per lane); a multiple of
     // SPLITS that divides 32, and at most STAGES
     static constexpr int ISSUE_W = STAGES >= 32 ? 32 : (STAGES >= 16 ? 16 : (STAGES >= 8 ? 8 : (STAGES >= 4 ? 4 : 2)));
@@ -493,7 +505,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int b_chk = (lane >> 3) & 1;
     constexpr int KS = D / 16;  // k-steps of QK^T, and 16-column pairs of PV
     constexpr int NT = D / 8;   // n-tiles of the O accumulator
-    uint32_t mycnt = 0;  // blocks this warp's split has consumed, over all windows
+    // Per-lane shared-memory offsets of this warp's head inside a tile, per
+    // 16-wide k-step: ldmatrix rows of K (B operand of Q K^T) and of V (B
+    // operand of P V, transposed), computed once.
+    uint32_t offk[KS], offv[KS];
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+        offk[ks] = swz128(chunk_row<C::HA>(hh * (D / 64) + ks / 4, b_row), (ks & 3) * 2 + b_chk);
+        offv[ks] = swz128(chunk_row<C::HA>(hh * (D / 64) + ks / 4, a_row), (ks & 3) * 2 + a_chk);
+    }
+    // position of this split's next block in its sub-ring (slot l % S_SUB
+    // and phase parity (l / S_SUB) & 1 of its l-th block over all windows)
+    uint32_t ring_pos = 0, ring_par = 0;
     for (int k = 0;; ++k) {
         const int q = k & 1;
         if (!wait_warp(qfull(q), (k >> 1) & 1, err, p.timeout_ns)) return;
@@ -525,14 +548,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         bool ok = true;
         auto qk_tile = [&](uint32_t kt, float (&sc)[2][4]) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) sc[0][i] = sc[1][i] = 0.f;
-#pragma unroll
             for (int ks = 0; ks < KS; ++ks) {
-                const uint32_t row = chunk_row<C::HA>(hh * (D / 64) + ks / 4, b_row);
                 uint32_t k0, k1, k2, k3;
-                ldsm_x4(kt + swz128(row, (ks & 3) * 2 + b_chk), k0, k1, k2, k3);
-                mma_16816(sc[0], qa[ks], k0, k1);
-                mma_16816(sc[1], qa[ks], k2, k3);
+                ldsm_x4(kt + offk[ks], k0, k1, k2, k3);
+                if (ks == 0) {
+                    mma_16816_zero(sc[0], qa[ks], k0, k1);
+                    mma_16816_zero(sc[1], qa[ks], k2, k3);
+                } else {
+                    mma_16816(sc[0], qa[ks], k0, k1);
+                    mma_16816(sc[1], qa[ks], k2, k3);
+                }
             }
         };
         auto mask_tail = [&](float (&sc)[2][4], int col) {
@@ -547,50 +572,53 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         auto pv_tile = [&](uint32_t vt, const uint32_t (&pa)[4]) {
 #pragma unroll
             for (int jj = 0; jj < KS; ++jj) {
-                const uint32_t row = chunk_row<C::HA>(hh * (D / 64) + jj / 4, a_row);
                 uint32_t v0, v1, v2, v3;
-                ldsm_x4_t(vt + swz128(row, (jj & 3) * 2 + a_chk), v0, v1, v2, v3);
+                ldsm_x4_t(vt + offv[jj], v0, v1, v2, v3);
                 mma_16816(o[2 * jj], pa, v0, v1);
                 mma_16816(o[2 * jj + 1], pa, v2, v3);
             }
         };
-        // Two blocks per step (this warp's j-th and (j+SPLITS)-th): their
-        // QK^T, exp and PV chains interleave, and one max update / rescale
-        // covers 32 columns.
-        // This split's blocks j = sp, sp + SPLITS, ... of the window are its
-        // local blocks mycnt, mycnt + 1, ...
-        // (d = 128 takes one block per step: its 64-register O accumulator
-        // leaves no room for a second block's scores under the 168-register
-        // budget of a 9-warp CTA)
-        constexpr int PAIR = D == 64 ? 2 : 1;
-        for (int j = sp; j < nb; j += PAIR * C::SPLITS) {
-            const bool two = PAIR == 2 && j + C::SPLITS < nb;  // warp-uniform
-            const uint32_t lc0 = mycnt + (uint32_t)(j - sp) / C::SPLITS, lc1 = lc0 + 1;
-            const uint32_t s0 = slot_of(sp, lc0), s1 = slot_of(sp, lc1);
-            float sc[2][2][4];
-            if (!wait_fast(full(s0), par_of(lc0), err, p.timeout_ns)) {
-                ok = false;
-                break;
-            }
-            qk_tile(kv_s + s0 * 2 * C::TILE, sc[0]);
-            if (two) {
-                if (!wait_fast(full(s1), par_of(lc1), err, p.timeout_ns)) {
-                    ok = false;
-                    break;
-                }
-                qk_tile(kv_s + s1 * 2 * C::TILE, sc[1]);
-            } else {
+        // NB blocks per step (this split's next NB blocks of the window, j,
+        // j + SPLITS, ...; the blocks j = sp, sp + SPLITS, ... are its next
+        // blocks in the sub-ring, in order): their QK^T, exp and P.V chains
+        // interleave, and one max update / rescale covers 16 * NB columns.
+        constexpr int NB = C::NB;
+        for (int j = sp; j < nb; j += NB * C::SPLITS) {
+            const int left = (nb - 1 - j) / C::SPLITS + 1;  // this split's blocks from j on
+            const int nblk = left < NB ? left : NB;          // warp-uniform
+            uint32_t st[NB], ph[NB];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) sc[1][0][i] = sc[1][1][i] = -INFINITY;
+            for (int b = 0; b < NB; ++b) {
+                st[b] = sp * C::S_SUB + ring_pos;
+                ph[b] = ring_par;
+                if (b < nblk && ++ring_pos == (uint32_t)C::S_SUB) {
+                    ring_pos = 0;
+                    ring_par ^= 1u;
+                }
             }
-            if (p.tail != 0) {
-                mask_tail(sc[0], stage_col[s0]);
-                if (two) mask_tail(sc[1], stage_col[s1]);
+            float sc[NB][2][4];
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                if (b < nblk) {
+                    if (!wait_fast(full(st[b]), ph[b], err, p.timeout_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    qk_tile(kv_s + st[b] * 2 * C::TILE, sc[b]);
+                    if (p.tail != 0) mask_tail(sc[b], stage_col[st[b]]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) sc[b][0][i] = sc[b][1][i] = -INFINITY;
+                }
             }
-            float mx0 = fmaxf(fmaxf(fmaxf(sc[0][0][0], sc[0][0][1]), fmaxf(sc[0][1][0], sc[0][1][1])),
-                              fmaxf(fmaxf(sc[1][0][0], sc[1][0][1]), fmaxf(sc[1][1][0], sc[1][1][1])));
-            float mx1 = fmaxf(fmaxf(fmaxf(sc[0][0][2], sc[0][0][3]), fmaxf(sc[0][1][2], sc[0][1][3])),
-                              fmaxf(fmaxf(sc[1][0][2], sc[1][0][3]), fmaxf(sc[1][1][2], sc[1][1][3])));
+            if (!ok) break;
+            float mx0 = fmaxf(fmaxf(sc[0][0][0], sc[0][0][1]), fmaxf(sc[0][1][0], sc[0][1][1]));
+            float mx1 = fmaxf(fmaxf(sc[0][0][2], sc[0][0][3]), fmaxf(sc[0][1][2], sc[0][1][3]));
+#pragma unroll
+            for (int b = 1; b < NB; ++b) {
+                mx0 = fmaxf(mx0, fmaxf(fmaxf(sc[b][0][0], sc[b][0][1]), fmaxf(sc[b][1][0], sc[b][1][1])));
+                mx1 = fmaxf(mx1, fmaxf(fmaxf(sc[b][0][2], sc[b][0][3]), fmaxf(sc[b][1][2], sc[b][1][3])));
+            }
             mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
             mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
             mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2)) * kLog2e;
@@ -611,34 +639,35 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 m0 = mn0;
                 m1 = mn1;
             }
-            uint32_t pa[2][4];
 #pragma unroll
-            for (int b = 0; b < 2; ++b) {
-                float pr[2][4];
+            for (int b = 0; b < NB; ++b) {
+                if (b < nblk) {
+                    float pr[2][4];
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                    pr[nt][0] = fast_exp2(fmaf(sc[b][nt][0], kLog2e, -m0));
-                    pr[nt][1] = fast_exp2(fmaf(sc[b][nt][1], kLog2e, -m0));
-                    pr[nt][2] = fast_exp2(fmaf(sc[b][nt][2], kLog2e, -m1));
-                    pr[nt][3] = fast_exp2(fmaf(sc[b][nt][3], kLog2e, -m1));
+                    for (int nt = 0; nt < 2; ++nt) {
+                        pr[nt][0] = fast_exp2(fmaf(sc[b][nt][0], kLog2e, -m0));
+                        pr[nt][1] = fast_exp2(fmaf(sc[b][nt][1], kLog2e, -m0));
+                        pr[nt][2] = fast_exp2(fmaf(sc[b][nt][2], kLog2e, -m1));
+                        pr[nt][3] = fast_exp2(fmaf(sc[b][nt][3], kLog2e, -m1));
+                    }
+                    l0 += (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
+                    l1 += (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
+                    uint32_t pa[4];
+                    pa[0] = pack_half2(pr[0][0], pr[0][1]);
+                    pa[1] = pack_half2(pr[0][2], pr[0][3]);
+                    pa[2] = pack_half2(pr[1][0], pr[1][1]);
+                    pa[3] = pack_half2(pr[1][2], pr[1][3]);
+                    pv_tile(kv_s + st[b] * 2 * C::TILE + C::TILE, pa);
                 }
-                l0 += (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
-                l1 += (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
-                pa[b][0] = pack_half2(pr[0][0], pr[0][1]);
-                pa[b][1] = pack_half2(pr[0][2], pr[0][3]);
-                pa[b][2] = pack_half2(pr[1][0], pr[1][1]);
-                pa[b][3] = pack_half2(pr[1][2], pr[1][3]);
             }
-            pv_tile(kv_s + s0 * 2 * C::TILE + C::TILE, pa[0]);
-            if (two) pv_tile(kv_s + s1 * 2 * C::TILE + C::TILE, pa[1]);
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(empty(s0));
-                if (two) mbar_arrive(empty(s1));
+#pragma unroll
+                for (int b = 0; b < NB; ++b)
+                    if (b < nblk) mbar_arrive(empty(st[b]));
             }
         }
         if (!ok) return;
-        mycnt += nb > sp ? (uint32_t)(nb - 1 - sp) / C::SPLITS + 1 : 0u;
         l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
         l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
         l0 += __shfl_xor_sync(0xffffffffu, l0, 2);

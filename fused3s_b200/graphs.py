@@ -180,6 +180,66 @@ def batched_er_graph(num_graphs: int = 4096, min_nodes: int = 20, max_nodes: int
     return csr_from_edges(n_total, u, v, "c3")
 
 
+def batched_er_graph_device(num_graphs: int = 4096, min_nodes: int = 20, max_nodes: int = 500,
+                            mean_degree: float = 8.0, self_loops: bool = True, seed: int = 3,
+                            device: str = "cuda", name: str = "c3") -> CSRGraph:
+    """C3 drawn on the device: the same family as batched_er_graph (sizes
+    uniform in [min_nodes, max_nodes], G(n, p) with p = mean_degree / (n - 1)
+    per graph, symmetrised, self-loops, block-diagonal), vectorised over all
+    graphs instead of a host loop per graph.  Every candidate pair (i < j) of
+    every graph is kept with its graph's p (so each graph's edge count is
+    Binomial(n (n - 1) / 2, p), as in the host version); a flat pair index is
+    mapped back to (graph, i, j) with a search over the graphs' pair offsets
+    and the inverse of the triangular numbering.  Deterministic for a seed
+    and device type; a different draw from batched_er_graph's."""
+    if torch is None:
+        raise RuntimeError("batched_er_graph_device needs torch")
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    sizes = torch.randint(min_nodes, max_nodes + 1, (num_graphs,), generator=gen, device=dev, dtype=torch.int64)
+    base = torch.cumsum(sizes, 0) - sizes                      # first node of each graph
+    pairs = sizes * (sizes - 1) // 2
+    poff = torch.cumsum(pairs, 0) - pairs                      # first flat pair of each graph
+    total = int(pairs.sum())
+    p = (mean_degree / (sizes - 1).clamp(min=1).to(torch.float64)).clamp(max=1.0)
+    us, vs = [], []
+    chunk = 1 << 26
+    for s0 in range(0, total, chunk):
+        idx = torch.arange(s0, min(total, s0 + chunk), device=dev, dtype=torch.int64)
+        gi = torch.searchsorted(poff, idx, right=True) - 1     # graph of each pair
+        keep = torch.rand(idx.shape[0], generator=gen, device=dev, dtype=torch.float64) < p[gi]
+        idx, gi = idx[keep], gi[keep]
+        t = idx - poff[gi]                                     # pair number inside the graph
+        n = sizes[gi]
+        # row i of pair t in the strict upper triangle, rows of lengths n-1, n-2, ...
+        b = (2 * n - 1).to(torch.float64)
+        i = torch.floor((b - torch.sqrt(b * b - 8.0 * t.to(torch.float64))) / 2).to(torch.int64)
+        first = i * (2 * n - i - 1) // 2                       # first pair of row i
+        i = torch.where(first > t, i - 1, i)                   # guard the float estimate
+        first = i * (2 * n - i - 1) // 2
+        nxt = (i + 1) * (2 * n - i - 2) // 2
+        i = torch.where(t >= nxt, i + 1, i)
+        first = i * (2 * n - i - 1) // 2
+        j = t - first + i + 1
+        us.append(base[gi] + i)
+        vs.append(base[gi] + j)
+    n_total = int(sizes.sum())
+    u = torch.cat(us) if us else torch.zeros(0, dtype=torch.int64, device=dev)
+    v = torch.cat(vs) if vs else torch.zeros(0, dtype=torch.int64, device=dev)
+    src, dst = torch.cat([u, v]), torch.cat([v, u])
+    if self_loops:
+        ids = torch.arange(n_total, device=dev, dtype=torch.int64)
+        src, dst = torch.cat([src, ids]), torch.cat([dst, ids])
+    key = torch.unique(src * n_total + dst, sorted=True)
+    rows = torch.div(key, n_total, rounding_mode="floor")
+    cols = (key - rows * n_total).to(torch.int32)
+    counts = torch.bincount(rows, minlength=n_total)
+    row_ptr = torch.zeros(n_total + 1, dtype=torch.int64, device=dev)
+    torch.cumsum(counts, 0, out=row_ptr[1:])
+    return CSRGraph(n_total, row_ptr.to(torch.int32).cpu().numpy(), cols.cpu().numpy(), name)
+
+
 # ----------------------------------------------------------------------------
 # C4 / C5 (R-MAT, torch on the given device)
 # ----------------------------------------------------------------------------
@@ -235,6 +295,8 @@ def make_graph(config: str, device: str = "cpu", seed: Optional[int] = None) -> 
     if config == "c2":
         return heavy_tailed_graph(**kw)
     if config == "c3":
+        if device != "cpu":  # drawn on the GPU (the host loop stays for CPU callers)
+            return batched_er_graph_device(device=device, **kw)
         return batched_er_graph(**kw)
     if config == "c4":
         return rmat_graph(20, 16, device=device, name="c4", **kw)

@@ -136,3 +136,28 @@ def test_overlapped_gather_two_gloo_ranks():
     for p in procs:
         p.join(timeout=60)
     assert sorted(results) == [(0, True), (1, True)]
+
+
+def test_device_er_generator_family():
+    """The vectorised C3 generator (batched_er_graph_device), run with torch
+    on the CPU: block-diagonal, symmetric, every self-loop, mean degree near
+    8 + 1, sizes in range, deterministic for a seed."""
+    from fused3s_b200 import graphs as G
+    g = G.batched_er_graph_device(num_graphs=200, device="cpu", seed=11)
+    g2 = G.batched_er_graph_device(num_graphs=200, device="cpu", seed=11)
+    assert np.array_equal(g.row_ptr, g2.row_ptr) and np.array_equal(g.col_ind, g2.col_ind)
+    rp, ci = g.row_ptr.astype(np.int64), g.col_ind.astype(np.int64)
+    deg = np.diff(rp)
+    assert 8.0 < deg.mean() < 10.0
+    rows = np.repeat(np.arange(g.num_nodes), deg)
+    edges = set(zip(rows.tolist(), ci.tolist()))
+    assert all((b, a) in edges for a, b in edges)
+    assert all((i, i) in edges for i in range(g.num_nodes))
+    # block diagonal: no edge crosses a component; components are 20..500 nodes
+    import scipy.sparse as sp
+    from scipy.sparse.csgraph import connected_components
+    A = sp.csr_matrix((np.ones(ci.shape[0]), ci, rp), shape=(g.num_nodes, g.num_nodes))
+    _, lab = connected_components(A, directed=False)
+    sizes = np.bincount(lab)
+    assert sizes.max() <= 500  # components stay inside one graph of at most 500 nodes
+    assert np.all(np.abs(rows - ci) < 500)  # graphs are laid out one after another
