@@ -601,18 +601,26 @@ def run_ours(args):
                                                    sub_slabs=args.sub_slabs, out_dtype=O.dtype, block_hints=hints,
                                                    plans=sub_plans, gather=og)
 
-        for _ in range(2):
-            fwd_gather()
-        dist.barrier()
-        torch.cuda.synchronize()
-        ge[2].record(stream)
-        for _ in range(args.steps):
-            fwd_gather()
-        ge[3].record(stream)
-        torch.cuda.synchronize()
-        t = torch.tensor([ge[2].elapsed_time(ge[3]) / args.steps], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        overlap_ms = float(t.item())
+        # the NCCL all-gather's kernels need SMs: time it with the forward
+        # leaving k SMs free (f3s_set_forward_sm_limit) for each k asked for
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        overlap_by_free = {}
+        for k in [int(x) for x in args.gather_free_sms.split(",")]:
+            F.set_forward_sm_limit(sms - k if k > 0 else 0, dev)
+            for _ in range(2):
+                fwd_gather()
+            dist.barrier()
+            torch.cuda.synchronize()
+            ge[2].record(stream)
+            for _ in range(args.steps):
+                fwd_gather()
+            ge[3].record(stream)
+            torch.cuda.synchronize()
+            t = torch.tensor([ge[2].elapsed_time(ge[3]) / args.steps], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            overlap_by_free[k] = float(t.item())
+        F.set_forward_sm_limit(0, dev)
+        overlap_ms = min(overlap_by_free.values())
         del og
         # (3) the same with the rows moved by the copy engines into IPC-mapped
         # peer buffers (no SMs taken from the fused kernel)
@@ -689,6 +697,7 @@ def run_ours(args):
             result["allgather_o_ms"] = gather_ms
             result["forward_then_allgather_ms"] = ms_per_step + gather_ms
             result["forward_allgather_overlapped_ms"] = overlap_ms
+            result["forward_allgather_overlapped_ms_by_free_sms"] = overlap_by_free
             result["forward_peer_copy_overlapped_ms"] = peer_ms
             result["sub_slabs"] = args.sub_slabs
         emit(result)
@@ -713,6 +722,8 @@ def main(argv=None):
     ap.add_argument("--graph-seed", type=int, default=None, help="seed of the graph (default: the configuration's)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gather", action="store_true", help="also time the NCCL all-gather of O (N > 1)")
+    ap.add_argument("--gather-free-sms", default="0,4,8",
+                    help="SMs the forward leaves free for the overlapped NCCL all-gather (comma list, --gather)")
     ap.add_argument("--sub-slabs", type=int, default=4,
                     help="sub-slabs per rank for the overlapped forward + all-gather (--gather)")
     ap.add_argument("--out-dtype", default="f32", choices=["f32", "f16", "bf16"], help="element type of O")

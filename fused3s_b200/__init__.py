@@ -27,6 +27,7 @@ from .api import (
     make_chunked_plan,
     make_sliced_plan,
     plan_merge,
+    set_forward_sm_limit,
     make_plan,
     parse_int32_text,
     workspace_status,
@@ -50,6 +51,7 @@ __all__ = [
     "load_plan",
     "make_sliced_plan",
     "plan_merge",
+    "set_forward_sm_limit",
     "float2half",
     "forward_workspace",
     "fused3s_forward",

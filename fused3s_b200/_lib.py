@@ -39,6 +39,7 @@ SIGNATURES = {
     "f3s_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "f3s_version": (ctypes.c_int, []),
     "f3s_last_cuda_error": (ctypes.c_int, []),
+    "f3s_set_forward_sm_limit": (ctypes.c_int, [_I32]),
     "f3s_workspace_status": (ctypes.c_int, [_P, _P]),
     "f3s_convert_workspace_size": (_SZ, [_I32, _I64]),
     "f3s_convert": (ctypes.c_int, [_P, _P, _I32, _I64, _P, _P, _P, _SZ, ctypes.POINTER(_I64), _P]),

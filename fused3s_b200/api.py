@@ -619,6 +619,15 @@ def plan_merge(plan: ForwardPlan, out: torch.Tensor, num_nodes: int, q_window_ba
     return out
 
 
+def set_forward_sm_limit(max_ctas: int, device=None) -> None:
+    """At most max_ctas persistent CTAs per forward launch on `device` from
+    now on (0: one per SM); leaves SMs to a kernel that runs beside the
+    forward, e.g. an NCCL all-gather on another stream."""
+    device = _default_device(device)
+    with torch.cuda.device(device):
+        check(_lib.load().f3s_set_forward_sm_limit(int(max_ctas)), "f3s_set_forward_sm_limit")
+
+
 def forward_workspace(device=None) -> torch.Tensor:
     """The workspace fused3s_forward uses on the current stream of `device`."""
     device = _default_device(device)

@@ -28,6 +28,27 @@ int num_sms_of_current_device() {
     return n;
 }
 
+// Upper bound on the persistent CTAs of a forward launch, per device (0: one
+// per SM).  Set by f3s_set_forward_sm_limit.
+static std::atomic<int> g_forward_sm_limit[kMaxDevices] = {};
+
+int forward_grid_limit() {
+    const int sms = num_sms_of_current_device();
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return sms;
+    const int lim = g_forward_sm_limit[dev].load(std::memory_order_relaxed);
+    return lim > 0 && lim < sms ? lim : sms;
+}
+
+int set_forward_sm_limit(int max_ctas) {
+    int dev = 0;
+    F3S_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return F3S_ERR_UNSUPPORTED;
+    if (max_ctas < 0) return F3S_ERR_INVALID_VALUE;
+    g_forward_sm_limit[dev].store(max_ctas, std::memory_order_relaxed);
+    return F3S_SUCCESS;
+}
+
 // Driver entry points for the context identity, looked up once through the
 // runtime (the library links no libcuda).
 using PfnCtxGetCurrent = CUresult (*)(CUcontext*);
@@ -119,7 +140,9 @@ const char* f3s_status_string(int status) {
     }
 }
 
-int f3s_version(void) { return 1 * 10000 + 0 * 100 + 0; }
+int f3s_version(void) { return 1 * 10000 + 1 * 100 + 0; }
+
+int f3s_set_forward_sm_limit(int32_t max_ctas) { return f3s::set_forward_sm_limit(max_ctas); }
 
 int f3s_last_cuda_error(void) { return f3s::g_last_cuda_error.load(); }
 

@@ -989,8 +989,9 @@ static int launch_variant(const void* Q, const void* K, const void* V, FwdParams
         !encode_map(&maps.va, V, kv_rows, prm.heads, D, C::HA) || !encode_map(&maps.vb, V, kv_rows, prm.heads, D, hb))
         return F3S_ERR_INVALID_VALUE;
     const int sms = num_sms_of_current_device();
+    const int ctas = forward_grid_limit();
     const int items = prm.num_items * prm.groups;
-    const int grid = prm.plan ? sms : std::max(1, std::min(items, sms));
+    const int grid = prm.plan ? ctas : std::max(1, std::min(items, ctas));
     k_fused3s<D, HG><<<grid, kFwdThreads, C::SMEM, stream>>>(maps, prm);
     F3S_LAUNCH_CHECK();
     if (prm.plan && merge) {

@@ -101,6 +101,8 @@ class PerContext {
     } while (0)
 
 int num_sms_of_current_device();
+// persistent CTAs a forward launch may use on the current device
+int forward_grid_limit();
 
 // NVTX range around an entry point's host side (its enqueue), named after
 // the call; free when no profiler is attached.

@@ -60,6 +60,13 @@ int f3s_version(void);
 /* Last CUDA error seen by a call that returned F3S_ERR_CUDA (cudaError_t). */
 int f3s_last_cuda_error(void);
 
+/* At most max_ctas persistent CTAs per forward launch on the current device
+ * from now on (0: one per SM, the default).  The fused kernel holds one CTA
+ * per SM for its whole run; a caller that overlaps it with another kernel
+ * -- an NCCL collective on a second stream, say -- leaves that kernel SMs
+ * this way.  No reference counterpart. */
+int f3s_set_forward_sm_limit(int32_t max_ctas);
+
 /* ------------------------------------------------------------------------
  * Workspace status.  Synchronises `stream`, returns the first error code a
  * kernel recorded in `d_workspace` (any of the workspaces below) and clears
