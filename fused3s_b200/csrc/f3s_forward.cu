@@ -88,12 +88,16 @@ struct FwdCfg {
     // the producer to keep loading (d = 128: one block, its O accumulator
     // is 64 registers).
 #ifndef F3S_BLOCKS_PER_STEP
-#define F3S_BLOCKS_PER_STEP 3
+#define F3S_BLOCKS_PER_STEP 2
 #endif
     static constexpr int NB_WANT = D == 64 ? F3S_BLOCKS_PER_STEP : 2;
-    static constexpr int NB_ROOM = S_SUB - 2 > 1 ? S_SUB - 2 : 1;  // keep two stages loading if possible
-    static constexpr int NB = NB_WANT < NB_ROOM ? NB_WANT : NB_ROOM;
-    static_assert(NB >= 1 && NB < S_SUB, "a step must leave the producer a stage");
+    // Software-pipelined steps hold two steps' stages (the next step's QK^T
+    // runs during this step's softmax and P.V): possible when 2 * NB stages
+    // still leave the producer one.  Otherwise one block per step, in order.
+    static constexpr int NB_PIPE = (S_SUB - 1) / 2 < NB_WANT ? (S_SUB - 1) / 2 : NB_WANT;
+    static constexpr bool PIPE = NB_PIPE >= 1;
+    static constexpr int NB = PIPE ? NB_PIPE : 1;
+    static_assert(NB >= 1 && (PIPE ? 2 * NB : NB) < S_SUB, "a step must leave the producer a stage");
     // blocks the producer issues per round (one per lane); a multiple of
     // SPLITS that divides 32, and at most STAGES
     static constexpr int ISSUE_W = STAGES >= 32 ? 32 : (STAGES >= 16 ? 16 : (STAGES >= 8 ? 8 : (STAGES >= 4 ? 4 : 2)));
@@ -583,41 +587,51 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         // blocks in the sub-ring, in order): their QK^T, exp and P.V chains
         // interleave, and one max update / rescale covers 16 * NB columns.
         constexpr int NB = C::NB;
-        for (int j = sp; j < nb; j += NB * C::SPLITS) {
+        constexpr int STEP = NB * C::SPLITS;
+        struct Step {
+            float sc[NB][2][4];
+            uint32_t st[NB];
+            int n;  // blocks in the step (0: past the window's end)
+        };
+        // Waits for the step's stages and issues its QK^T.
+        auto fetch = [&](Step& S, int j) -> bool {
+            if (j >= nb) {
+                S.n = 0;
+                return true;
+            }
             const int left = (nb - 1 - j) / C::SPLITS + 1;  // this split's blocks from j on
-            const int nblk = left < NB ? left : NB;          // warp-uniform
-            uint32_t st[NB], ph[NB];
+            S.n = left < NB ? left : NB;                     // warp-uniform
+            uint32_t ph[NB];
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
-                st[b] = sp * C::S_SUB + ring_pos;
+                S.st[b] = sp * C::S_SUB + ring_pos;
                 ph[b] = ring_par;
-                if (b < nblk && ++ring_pos == (uint32_t)C::S_SUB) {
+                if (b < S.n && ++ring_pos == (uint32_t)C::S_SUB) {
                     ring_pos = 0;
                     ring_par ^= 1u;
                 }
             }
-            float sc[NB][2][4];
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
-                if (b < nblk) {
-                    if (!wait_fast(full(st[b]), ph[b], err, p.timeout_ns)) {
-                        ok = false;
-                        break;
-                    }
-                    qk_tile(kv_s + st[b] * 2 * C::TILE, sc[b]);
-                    if (p.tail != 0) mask_tail(sc[b], stage_col[st[b]]);
+                if (b < S.n) {
+                    if (!wait_fast(full(S.st[b]), ph[b], err, p.timeout_ns)) return false;
+                    qk_tile(kv_s + S.st[b] * 2 * C::TILE, S.sc[b]);
+                    if (p.tail != 0) mask_tail(S.sc[b], stage_col[S.st[b]]);
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) sc[b][0][i] = sc[b][1][i] = -INFINITY;
+                    for (int i = 0; i < 4; ++i) S.sc[b][0][i] = S.sc[b][1][i] = -INFINITY;
                 }
             }
-            if (!ok) break;
-            float mx0 = fmaxf(fmaxf(sc[0][0][0], sc[0][0][1]), fmaxf(sc[0][1][0], sc[0][1][1]));
-            float mx1 = fmaxf(fmaxf(sc[0][0][2], sc[0][0][3]), fmaxf(sc[0][1][2], sc[0][1][3]));
+            return true;
+        };
+        // Softmax update and P.V of a fetched step; frees its stages.
+        auto process = [&](Step& S) {
+            float mx0 = fmaxf(fmaxf(S.sc[0][0][0], S.sc[0][0][1]), fmaxf(S.sc[0][1][0], S.sc[0][1][1]));
+            float mx1 = fmaxf(fmaxf(S.sc[0][0][2], S.sc[0][0][3]), fmaxf(S.sc[0][1][2], S.sc[0][1][3]));
 #pragma unroll
             for (int b = 1; b < NB; ++b) {
-                mx0 = fmaxf(mx0, fmaxf(fmaxf(sc[b][0][0], sc[b][0][1]), fmaxf(sc[b][1][0], sc[b][1][1])));
-                mx1 = fmaxf(mx1, fmaxf(fmaxf(sc[b][0][2], sc[b][0][3]), fmaxf(sc[b][1][2], sc[b][1][3])));
+                mx0 = fmaxf(mx0, fmaxf(fmaxf(S.sc[b][0][0], S.sc[b][0][1]), fmaxf(S.sc[b][1][0], S.sc[b][1][1])));
+                mx1 = fmaxf(mx1, fmaxf(fmaxf(S.sc[b][0][2], S.sc[b][0][3]), fmaxf(S.sc[b][1][2], S.sc[b][1][3])));
             }
             mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
             mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
@@ -641,14 +655,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             }
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
-                if (b < nblk) {
+                if (b < S.n) {
                     float pr[2][4];
 #pragma unroll
                     for (int nt = 0; nt < 2; ++nt) {
-                        pr[nt][0] = fast_exp2(fmaf(sc[b][nt][0], kLog2e, -m0));
-                        pr[nt][1] = fast_exp2(fmaf(sc[b][nt][1], kLog2e, -m0));
-                        pr[nt][2] = fast_exp2(fmaf(sc[b][nt][2], kLog2e, -m1));
-                        pr[nt][3] = fast_exp2(fmaf(sc[b][nt][3], kLog2e, -m1));
+                        pr[nt][0] = fast_exp2(fmaf(S.sc[b][nt][0], kLog2e, -m0));
+                        pr[nt][1] = fast_exp2(fmaf(S.sc[b][nt][1], kLog2e, -m0));
+                        pr[nt][2] = fast_exp2(fmaf(S.sc[b][nt][2], kLog2e, -m1));
+                        pr[nt][3] = fast_exp2(fmaf(S.sc[b][nt][3], kLog2e, -m1));
                     }
                     l0 += (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
                     l1 += (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
@@ -657,14 +671,36 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     pa[1] = pack_half2(pr[0][2], pr[0][3]);
                     pa[2] = pack_half2(pr[1][0], pr[1][1]);
                     pa[3] = pack_half2(pr[1][2], pr[1][3]);
-                    pv_tile(kv_s + st[b] * 2 * C::TILE + C::TILE, pa);
+                    pv_tile(kv_s + S.st[b] * 2 * C::TILE + C::TILE, pa);
                 }
             }
             __syncwarp();
             if (lane == 0) {
 #pragma unroll
                 for (int b = 0; b < NB; ++b)
-                    if (b < nblk) mbar_arrive(empty(st[b]));
+                    if (b < S.n) mbar_arrive(empty(S.st[b]));
+            }
+        };
+        if constexpr (C::PIPE) {
+            // two steps in flight: fetch(next) issues its QK^T before
+            // process(current) -- same steps, same order of arithmetic
+            Step A, B;
+            int j = sp;
+            ok = fetch(A, j);
+            while (ok && A.n > 0) {
+                if (!(ok = fetch(B, j + STEP))) break;
+                process(A);
+                j += STEP;
+                if (B.n == 0) break;
+                if (!(ok = fetch(A, j + STEP))) break;
+                process(B);
+                j += STEP;
+            }
+        } else {
+            Step A;
+            for (int j = sp; j < nb; j += STEP) {
+                if (!(ok = fetch(A, j))) break;
+                process(A);
             }
         }
         if (!ok) return;
