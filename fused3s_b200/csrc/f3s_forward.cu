@@ -85,19 +85,16 @@ struct FwdCfg {
     // Blocks a consumer warp takes per step (one max update and one vote per
     // step; their QK^T / exp / P.V chains interleave).  A step holds NB
     // stages of the split's sub-ring until its end, so NB leaves stages for
-    // the producer to keep loading (d = 128: one block, its O accumulator
-    // is 64 registers).
+    // the producer to keep loading.  Measured on B200 (C1 / C3 / c4s / C4):
+    // 2 is fastest; 3 ties; 4 is slower; issuing the next step's QK^T before
+    // this step's softmax (two steps in flight) was slower too.
 #ifndef F3S_BLOCKS_PER_STEP
 #define F3S_BLOCKS_PER_STEP 2
 #endif
     static constexpr int NB_WANT = D == 64 ? F3S_BLOCKS_PER_STEP : 2;
-    // Software-pipelined steps hold two steps' stages (the next step's QK^T
-    // runs during this step's softmax and P.V): possible when 2 * NB stages
-    // still leave the producer one.  Otherwise one block per step, in order.
-    static constexpr int NB_PIPE = (S_SUB - 1) / 2 < NB_WANT ? (S_SUB - 1) / 2 : NB_WANT;
-    static constexpr bool PIPE = NB_PIPE >= 1;
-    static constexpr int NB = PIPE ? NB_PIPE : 1;
-    static_assert(NB >= 1 && (PIPE ? 2 * NB : NB) < S_SUB, "a step must leave the producer a stage");
+    static constexpr int NB_ROOM = S_SUB - 2 > 1 ? S_SUB - 2 : 1;  // keep two stages loading if possible
+    static constexpr int NB = NB_WANT < NB_ROOM ? NB_WANT : NB_ROOM;
+    static_assert(NB >= 1 && NB < S_SUB, "a step must leave the producer a stage");
     // blocks the producer issues per round (one per lane); a multiple of
     // SPLITS that divides 32, and at most STAGES
     static constexpr int ISSUE_W = STAGES >= 32 ? 32 : (STAGES >= 16 ? 16 : (STAGES >= 8 ? 8 : (STAGES >= 4 ? 4 : 2)));
@@ -681,27 +678,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     if (b < S.n) mbar_arrive(empty(S.st[b]));
             }
         };
-        if constexpr (C::PIPE) {
-            // two steps in flight: fetch(next) issues its QK^T before
-            // process(current) -- same steps, same order of arithmetic
-            Step A, B;
-            int j = sp;
-            ok = fetch(A, j);
-            while (ok && A.n > 0) {
-                if (!(ok = fetch(B, j + STEP))) break;
-                process(A);
-                j += STEP;
-                if (B.n == 0) break;
-                if (!(ok = fetch(A, j + STEP))) break;
-                process(B);
-                j += STEP;
-            }
-        } else {
-            Step A;
-            for (int j = sp; j < nb; j += STEP) {
-                if (!(ok = fetch(A, j))) break;
-                process(A);
-            }
+        Step A;
+        for (int j = sp; j < nb; j += STEP) {
+            if (!(ok = fetch(A, j))) break;
+            process(A);
         }
         if (!ok) return;
         l0 += __shfl_xor_sync(0xffffffffu, l0, 1);

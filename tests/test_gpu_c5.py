@@ -10,9 +10,11 @@ reference's own functions):
   * the window order (the stable order exactly; the reference's block-count
     sequence when the compiled reference is present);
   * the fused output of the bench's configuration (automatic plan, L2
-    hints) on 128 seeded random windows x all heads, and on the 3 heaviest
-    windows (hub windows of several hundred thousand blocks) x the first and
-    last head, at max-abs 2e-2 / rel-L2 1e-3.
+    hints) on 128 seeded random windows x all heads against the reference's
+    float32 CPU function, and on the 3 heaviest windows (hub windows of
+    several hundred thousand blocks) x the first and last head against the
+    same block semantics in float64 (the float32 reference's softmax sum
+    drifts over millions of columns), at max-abs 2e-2 / rel-L2 1e-3.
 About 90 GB of device memory and a few minutes of host time.
 """
 import os
@@ -75,7 +77,25 @@ def test_c5_fused_output_sampled(lib, c5):
     got, want = oracle.sampled_check(N, off, cols, rand, Q, K, V, O, threads=THREADS)
     ma, rl = oracle.max_abs(got, want), oracle.rel_l2(got, want)
     assert ma <= MAX_ABS_TOL and rl <= REL_L2_TOL, f"random windows: maxabs={ma:.3e} relL2={rl:.3e}"
-    heavy = np.argsort(-cnt, kind="stable")[:3]
-    got, want = oracle.sampled_check(N, off, cols, np.sort(heavy), Q, K, V, O, heads=[0, H - 1], threads=THREADS)
-    ma, rl = oracle.max_abs(got, want), oracle.rel_l2(got, want)
+    # The 3 heaviest windows hold several hundred thousand blocks (millions
+    # of columns per row).  There the reference's float32 softmax sum, added
+    # column by column, drifts (its adds round to the accumulator's ulp), so
+    # the yardstick is the same block semantics in float64
+    # (oracle.block_attention_exact); the float32 reference's own distance
+    # from it is reported beside ours.
+    heavy = np.sort(np.argsort(-cnt, kind="stable")[:3])
+    got, ref32 = oracle.sampled_check(N, off, cols, heavy, Q, K, V, O, heads=[0, H - 1], threads=THREADS)
+    exact = []
+    for w in heavy:
+        rows = torch.arange(16 * w, min(16 * w + 16, N), device=Q.device)
+        exact.append(np.stack([oracle.block_attention_exact(N, Q[rows, h, :].float().cpu().numpy(), K[:, h, :],
+                                                            V[:, h, :], off, cols, int(w))
+                               for h in (0, H - 1)], axis=1))
+    exact = np.concatenate(exact)
+    ma, rl = oracle.max_abs(got, exact), oracle.rel_l2(got, exact)
+    print(f"heaviest windows {cnt[heavy].tolist()} blocks: fused vs float64 maxabs={ma:.3e} relL2={rl:.3e}; "
+          f"float32 reference vs float64 maxabs={oracle.max_abs(ref32, exact):.3e} "
+          f"relL2={oracle.rel_l2(ref32, exact):.3e}")
     assert ma <= MAX_ABS_TOL and rl <= REL_L2_TOL, f"heaviest windows: maxabs={ma:.3e} relL2={rl:.3e}"
+    # and within the max-abs bar of the float32 reference itself
+    assert oracle.max_abs(got, ref32) <= MAX_ABS_TOL

@@ -175,3 +175,18 @@ def test_compact_windows_is_bit_identical_to_the_full_problem(n):
             rows = np.arange(16 * w, min(16 * w + 16, n))
             crows = 16 * int(wc) + np.arange(rows.shape[0])
             assert np.array_equal(oc[crows], full[rows]), w
+
+
+def test_exact_restatement_agrees_with_the_port():
+    """oracle.block_attention_exact (float64, chunked) and the float32 port
+    agree on ordinary windows, the masked tail included."""
+    n = 16 * 60 + 7
+    rng = np.random.default_rng(2)
+    g = G.csr_from_edges(n, rng.integers(0, n, 3000), rng.integers(0, n, 3000))
+    off, cols = oracle.convert(n, g.row_ptr, g.col_ind)
+    q, k, v = (x.float().numpy() for x in G.make_features(n, 1, 64, kind="uniform", seed=4))
+    ref = oracle.block_attention(n, q, k, v, off, cols)
+    for w in (0, 17, len(off) - 2):
+        rows = np.arange(16 * w, min(16 * w + 16, n))
+        ex = oracle.block_attention_exact(n, q[rows, 0], k[:, 0], v[:, 0], off, cols, w, chunk=333)
+        assert oracle.max_abs(ref[rows, 0], ex) < 1e-5
