@@ -24,6 +24,7 @@ from .api import (
     column_slices,
     forward_pieces,
     load_plan,
+    locality_order,
     make_chunked_plan,
     make_sliced_plan,
     plan_merge,
@@ -49,6 +50,7 @@ __all__ = [
     "column_slices",
     "forward_pieces",
     "load_plan",
+    "locality_order",
     "make_sliced_plan",
     "plan_merge",
     "set_forward_sm_limit",

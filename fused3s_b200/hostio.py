@@ -73,12 +73,14 @@ class HostForward:
     run(hQ, hK, hV, hO): hQ = the range's Q rows [q_rows, H, d] fp16, hK / hV
     = this caller's K / V rows (all of them, or its share), hO = [q_rows, H, d]
     of out_dtype; all pinned host tensors.  Enqueued on the current stream
-    (which waits for the copy streams at the end); returns hO."""
+    (which waits for the copy streams at the end); returns hO.
+    buffers: optional (dQ, dK, dV, dO) device tensors to use instead of
+    allocating them (their contents are overwritten every run)."""
 
     def __init__(self, fmt: F.BlockSparseFormat, heads: int, head_dim: int, order: Optional[torch.Tensor] = None,
                  window_range: Optional[Tuple[int, int]] = None, kv_share: Optional[Tuple[int, int]] = None,
                  block_hints: Optional[torch.Tensor] = None, sub_slabs: int = 4,
-                 out_dtype: torch.dtype = torch.float32, group=None):
+                 out_dtype: torch.dtype = torch.float32, group=None, buffers=None):
         self.fmt, self.heads, self.head_dim = fmt, heads, head_dim
         self.device = fmt.window_offsets.device
         N = fmt.num_nodes
@@ -108,10 +110,20 @@ class HostForward:
         self.rank, self.world = rank, world
         shape = (heads, head_dim)
         dev = self.device
-        self.dQ = torch.empty((self.r1 - self.r0,) + shape, dtype=torch.float16, device=dev)
-        self.dK = torch.empty((max(kv_rows, 1),) + shape, dtype=torch.float16, device=dev)
-        self.dV = torch.empty((max(kv_rows, 1),) + shape, dtype=torch.float16, device=dev)
-        self.dO = torch.empty((self.r1 - self.r0,) + shape, dtype=out_dtype, device=dev)
+        if buffers is not None:
+            # the caller's device buffers (Q slab, K, V with kv_rows rows, O
+            # slab): reused instead of allocated -- at C5's size one set of
+            # device buffers is half the GPU's memory
+            self.dQ, self.dK, self.dV, self.dO = buffers
+            if (tuple(self.dQ.shape) != (self.r1 - self.r0,) + shape or self.dK.shape[0] < max(kv_rows, 1)
+                    or self.dV.shape[0] < max(kv_rows, 1) or tuple(self.dO.shape) != (self.r1 - self.r0,) + shape
+                    or self.dO.dtype != out_dtype):
+                raise ValueError("buffers do not fit the window range / K / V rows / O type")
+        else:
+            self.dQ = torch.empty((self.r1 - self.r0,) + shape, dtype=torch.float16, device=dev)
+            self.dK = torch.empty((max(kv_rows, 1),) + shape, dtype=torch.float16, device=dev)
+            self.dV = torch.empty((max(kv_rows, 1),) + shape, dtype=torch.float16, device=dev)
+            self.dO = torch.empty((self.r1 - self.r0,) + shape, dtype=out_dtype, device=dev)
         self.s_in = torch.cuda.Stream(dev)
         self.s_out = torch.cuda.Stream(dev)
 
