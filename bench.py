@@ -420,13 +420,20 @@ def run_ours(args):
     if args.split != "off":
         my_blocks_total = int((fmt.window_offsets[1:] - fmt.window_offsets[:-1])[lo:hi].sum().item())
         chunked = args.split.startswith("chunked")
-        if args.split == "auto" or chunked:
+        if args.split == "auto" or chunked or args.split.startswith("sweep"):
             T = F.auto_piece_blocks(my_blocks_total, dev)
         else:
             T = int(args.split)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        if chunked:
+        if args.split.startswith("sweep"):
+            # sweep plan: windows cut at block-column chunks, the chunks swept
+            # in order, one running state per window ("sweep" or
+            # "sweep:<block columns per chunk>")
+            chunk_cols = int(args.split.split(":")[1]) if ":" in args.split else None
+            plan = F.make_sweep_plan(fmt, H, d, order=my_order, chunk_cols=chunk_cols, window_range=(lo, hi))
+            ws = torch.zeros(lib.f3s_sweep_workspace_size(r1 - r0, H), dtype=torch.uint8, device=dev)
+        elif chunked:
             # column-chunked plan: all SMs sweep one L2-sized range of block
             # columns at a time ("chunked" or "chunked:<block columns>")
             chunk_cols = int(args.split.split(":")[1]) if ":" in args.split else None
@@ -755,8 +762,10 @@ def main(argv=None):
     ap.add_argument("--graph", default="on", choices=["on", "off"],
                     help="replay the timed step as a CUDA graph")
     ap.add_argument("--split", default="auto",
-                    help="cut windows above this many blocks into pieces: auto, off, a number, or "
-                         "chunked[:block columns] (pieces cut at column-chunk boundaries, swept chunk by chunk)")
+                    help="cut windows above this many blocks into pieces: auto, off, a number, "
+                         "chunked[:block columns] (pieces cut at column-chunk boundaries, swept chunk by chunk, "
+                         "partial states merged after), or sweep[:block columns] (the same schedule with one "
+                         "running state per window)")
     ap.add_argument("--l2-hints", default="on", choices=["on", "off"],
                     help="per block L2 eviction hints (computed once per graph)")
     ap.add_argument("--order", default="balanced", choices=["balanced", "local"],

@@ -27,6 +27,7 @@ from .api import (
     locality_order,
     make_chunked_plan,
     make_sliced_plan,
+    make_sweep_plan,
     plan_merge,
     set_forward_sm_limit,
     make_plan,
@@ -52,6 +53,7 @@ __all__ = [
     "load_plan",
     "locality_order",
     "make_sliced_plan",
+    "make_sweep_plan",
     "plan_merge",
     "set_forward_sm_limit",
     "float2half",

@@ -65,6 +65,9 @@ SIGNATURES = {
     "f3s_forward_pieces": (ctypes.c_int, [_P, _P, _P, _P, _I32, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
                                           _I32, _I32, _I32, _P, _SZ, _P]),
     "f3s_plan_merge": (ctypes.c_int, [_P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P]),
+    "f3s_sweep_plan_size": (_SZ, [_I32, _I32, _I32, _I32]),
+    "f3s_sweep_workspace_size": (_SZ, [_I32, _I32]),
+    "f3s_load_sweep_plan": (ctypes.c_int, [_P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _P, _SZ, _P]),
     "f3s_block_hints_workspace_size": (_SZ, [_I32]),
     "f3s_block_hints": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I64, _I64, _P, _P, _SZ, _P]),
     "f3s_1tb1rw_launch": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _P]),

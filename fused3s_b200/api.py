@@ -329,12 +329,14 @@ class ForwardPlan:
     """Device-resident work plan (f3s_make_plan): the listed windows in
     order, heavy ones cut into pieces of at most `max_blocks` blocks.
     piece_ranges: for a plan cut at K / V slice boundaries (make_sliced_plan),
-    the [begin, end) pieces of each slice."""
+    the [begin, end) pieces of each slice.  sweep: a window's pieces run in
+    sequence within one launch, carrying its running state (make_sweep_plan)."""
     buffer: torch.Tensor
     heads: int
     head_dim: int
     max_blocks: int
     piece_ranges: Optional[list] = None
+    sweep: bool = False  # a sweep plan (make_sweep_plan): needs the larger workspace
 
 
 # Longest run of blocks one work item accumulates.  The tensor cores add each
@@ -507,6 +509,40 @@ def load_plan(fmt: BlockSparseFormat, pieces: np.ndarray, splits: np.ndarray, n_
     return ForwardPlan(buf, heads, head_dim, int(max_blocks), piece_ranges)
 
 
+def make_sweep_plan(fmt: BlockSparseFormat, heads: int, head_dim: int, order: Optional[torch.Tensor] = None,
+                    chunk_cols: Optional[int] = None, l2_fraction: float = 1.0, window_range=None) -> ForwardPlan:
+    """A sweep plan (f3s_load_sweep_plan): every listed window cut where its
+    block columns cross a multiple of `chunk_cols`, the pieces ordered chunk by
+    chunk (windows in `order` within a chunk), so all SMs read one range of
+    K / V at a time and the L2 serves the rest of the chunk's reads; a window
+    carries its running softmax state from piece to piece (no partial state
+    per piece, no merge).  chunk_cols defaults to the block columns whose K
+    and V tiles fill `l2_fraction` of the device's L2.  window_range: the
+    slab (lo, hi) whose windows `order` lists (default all windows)."""
+    lib = _lib.load()
+    device = fmt.window_offsets.device
+    if order is None:
+        order = generate_balanced_window_order(fmt)
+    off, cols = fmt.to_host()
+    order_h = order.cpu().numpy().astype(np.int64)
+    if chunk_cols is None:
+        l2 = torch.cuda.get_device_properties(device).L2_cache_size
+        chunk_cols = max(1, int(l2 * l2_fraction) // (16 * heads * head_dim * 2 * 2))
+    pieces, _, _, _ = column_chunk_pieces(off, cols, order_h, int(chunk_cols), 0)
+    lo, hi = window_range if window_range is not None else (0, fmt.num_row_windows)
+    pieces = np.ascontiguousarray(pieces, dtype=np.int32)
+    size = lib.f3s_sweep_plan_size(pieces.shape[0], hi - lo, heads, head_dim)
+    if size == 0:
+        raise ValueError("unsupported plan parameters")
+    buf = torch.empty(size, dtype=torch.uint8, device=device)
+    off32 = np.ascontiguousarray(off.astype(np.int32))
+    with torch.cuda.device(device):
+        st = lib.f3s_load_sweep_plan(pieces.ctypes.data, pieces.shape[0], off32.ctypes.data, fmt.num_row_windows,
+                                     lo, hi - lo, heads, head_dim, _ptr(buf), size, _stream_ptr(device))
+    check(st, "f3s_load_sweep_plan")
+    return ForwardPlan(buf, heads, head_dim, int(chunk_cols), sweep=True)
+
+
 def column_slices(num_nodes: int, parts: int):
     """K / V cut into `parts` slices of whole block columns: boundaries
     col_cuts[0] = 0 < ... < col_cuts[parts] = ceil(num_nodes / 16) (equal
@@ -587,7 +623,9 @@ def fused3s_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, fmt: Bloc
         raise ValueError("out must be a contiguous tensor shaped like Q")
     if out.dtype not in _OUT_DTYPES:
         raise ValueError("O must be float32, float16 or bfloat16")
-    ws = _WS.get(device, "forward", lib.f3s_forward_workspace_size())
+    ws_bytes = (lib.f3s_sweep_workspace_size(q_rows, heads) if plan is not None and plan.sweep
+                else lib.f3s_forward_workspace_size())
+    ws = _WS.get(device, "forward", ws_bytes)
     with torch.cuda.device(device):
         st = lib.f3s_forward_ex(_ptr(Q), _ptr(K), _ptr(V), _ptr(out), _OUT_DTYPES[out.dtype],
                                 _ptr(fmt.window_offsets), fmt.cols_ptr, _ptr(order), _ptr(block_hints),

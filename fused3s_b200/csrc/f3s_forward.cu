@@ -129,9 +129,23 @@ struct PlanHeader {
     int status;            // 0, or an f3s_status if the plan overflowed
     long long splits_off;  // byte offsets of the sections; pieces follow the header
     long long partials_off;
-    int pad[48];
+    long long states_off;  // sweep plans: one running (m, l, O) state per window and head
+    int mode;              // kPlanPieces, or kPlanSweep
+    int pad[45];
 };
 static_assert(sizeof(PlanHeader) == 256, "plan header is 256 bytes");
+
+// Plan modes.  kPlanPieces: a split window's pieces write partial states
+// into their own slots, merged after the kernel (k_merge_pieces).
+// kPlanSweep: a window's pieces run one after another (each waits for the
+// previous one), carrying one running state per window and head: a piece
+// loads it, folds in its own blocks and stores it back; the last writes O.
+constexpr int kPlanPieces = 0;
+constexpr int kPlanSweep = 1;
+// piece info of a sweep plan: index of the piece within its window, and a
+// flag for the window's last piece
+constexpr int kSweepLast = 1 << 30;
+constexpr int kSweepIndexMask = kSweepLast - 1;
 
 struct FwdParams {
     void* O;            // [q_rows, H, D] of o_dtype
@@ -156,6 +170,8 @@ struct FwdParams {
     int piece_end;         // with a plan: end of the launch's pieces, or -1 for all
     int kv_col_base;       // first block column held in K / V (row 16 * kv_col_base of the graph)
     int kv_cols;           // block columns held in K / V
+    int* seq;              // sweep plans: per window and head, pieces of the window done this launch
+    long long seq_cap;     // entries of seq
 };
 
 // O stores: fp32 as computed, or rounded to nearest into fp16 / bf16.
@@ -518,6 +534,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // position of this split's next block in its sub-ring (slot l % S_SUB
     // and phase parity (l / S_SUB) & 1 of its l-th block over all windows)
     uint32_t ring_pos = 0, ring_par = 0;
+    const bool sweep = p.plan != nullptr && p.plan->mode == kPlanSweep;
+    constexpr int SE = NT * 4 + 4;  // floats of one lane's running state (O fragments, m0, l0, m1, l1)
     for (int k = 0;; ++k) {
         const int q = k & 1;
         if (!wait_warp(qfull(q), (k >> 1) & 1, err, p.timeout_ns)) return;
@@ -726,7 +744,59 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             if (lane == 0) mbar_arrive(mempty);
         }
 
-        if (pslot >= 0) {
+        if (sweep) {
+            // Sweep plan: the window's running state (this warp's head) is
+            // carried from piece to piece.  Piece k > 0 waits for piece k - 1
+            // (an earlier ticket, so it is running or done), folds the stored
+            // state in with the same max / scale rule as the split merge, and
+            // either stores the state back and releases piece k + 1, or, as
+            // the last piece, normalises and writes O below.
+            const int kpiece = pslot & kSweepIndexMask;
+            const bool last = (pslot & kSweepLast) != 0;
+            const long long fidx = ((long long)(w - p.q_window_base) * p.groups + g) * HG + hh;
+            if (fidx >= p.seq_cap) {
+                if (lane == 0) raise_error(err, F3S_ERR_BAD_FORMAT);
+                return;
+            }
+            int* flag = p.seq + fidx;
+            float4* st4 = reinterpret_cast<float4*>(reinterpret_cast<char*>(p.plan) + p.plan->states_off) +
+                          fidx * (SE / 4) * 32;
+            if (kpiece > 0) {
+                int okw = 1;
+                if (lane == 0) okw = flag_wait_bounded(flag, kpiece, err, p.timeout_ns) ? 1 : 0;
+                okw = __shfl_sync(0xffffffffu, okw, 0);
+                if (!okw) return;
+                __syncwarp();
+                const float4 ml = __ldcs(st4 + NT * 32 + lane);  // (m0, l0, m1, l1) of the pieces before
+                const float M0 = fmaxf(m0, ml.x), M1 = fmaxf(m1, ml.z);
+                const float a0 = fast_exp2(ml.x - M0), b0s = fast_exp2(m0 - M0);
+                const float a1 = fast_exp2(ml.z - M1), b1s = fast_exp2(m1 - M1);
+                l0 = ml.y * a0 + l0 * b0s;
+                l1 = ml.w * a1 + l1 * b1s;
+                m0 = M0;
+                m1 = M1;
+#pragma unroll
+                for (int jn = 0; jn < NT; ++jn) {
+                    const float4 v = __ldcs(st4 + jn * 32 + lane);
+                    o[jn][0] = v.x * a0 + o[jn][0] * b0s;
+                    o[jn][1] = v.y * a0 + o[jn][1] * b0s;
+                    o[jn][2] = v.z * a1 + o[jn][2] * b1s;
+                    o[jn][3] = v.w * a1 + o[jn][3] * b1s;
+                }
+            }
+            if (!last) {
+#pragma unroll
+                for (int jn = 0; jn < NT; ++jn)
+                    __stcs(st4 + jn * 32 + lane, make_float4(o[jn][0], o[jn][1], o[jn][2], o[jn][3]));
+                __stcs(st4 + NT * 32 + lane, make_float4(m0, l0, m1, l1));
+                __syncwarp();
+                if (lane == 0) {
+                    __threadfence();
+                    st_release_gpu(flag, kpiece + 1);
+                }
+                continue;
+            }
+        } else if (pslot >= 0) {
             // piece of a split window: partial (m, l, unnormalised O) of the
             // 16 rows and this warp's head -> plan scratch, merged later
             float* partials = reinterpret_cast<float*>(reinterpret_cast<char*>(p.plan) + p.plan->partials_off);
@@ -1159,6 +1229,84 @@ int load_plan_impl(const int32_t* pieces, int num_pieces, const int32_t* splits,
     return F3S_SUCCESS;
 }
 
+// Sweep plans: header, pieces (window, first block, end block, info), and
+// the running states (per window of the slab, head group and head: 32 lanes
+// x (head_dim / 2 + 4) floats, the consumer warp's O fragments and m / l).
+struct SweepPlanLayout {
+    size_t pieces, states, total;
+    int groups, hg;
+};
+
+static SweepPlanLayout sweep_plan_layout(int num_pieces, int q_windows, int heads, int head_dim) {
+    SweepPlanLayout L{};
+    L.hg = pick_head_group(heads, head_dim);
+    L.groups = heads / L.hg;
+    size_t off = sizeof(PlanHeader);
+    L.pieces = off;
+    off = align_up(off + (size_t)std::max(num_pieces, 1) * 16, 256);
+    L.states = off;
+    const size_t lane_floats = (size_t)head_dim / 2 + 4;  // NT * 4 + 4 with NT = head_dim / 8
+    off = align_up(off + (size_t)std::max(q_windows, 1) * heads * 32 * lane_floats * 4, 256);
+    L.total = off;
+    return L;
+}
+
+// A window's pieces must appear in the plan in ascending column order and
+// cover its blocks exactly once; each gets its index within the window and
+// the last one a flag.  Windows outside the slab are rejected.
+int load_sweep_plan_impl(const int32_t* pieces, int num_pieces, const int32_t* offsets, int nrw, int q_window_base,
+                         int q_windows, int heads, int head_dim, void* plan, size_t plan_bytes, cudaStream_t stream) {
+    if (num_pieces < 0 || nrw < 0 || heads <= 0 || q_window_base < 0 || q_windows < 0) return F3S_ERR_INVALID_VALUE;
+    if (head_dim != 64 && head_dim != 128) return F3S_ERR_UNSUPPORTED;
+    if (!plan || (num_pieces > 0 && (!pieces || !offsets))) return F3S_ERR_INVALID_VALUE;
+    if ((reinterpret_cast<uintptr_t>(plan) & 255) != 0) return F3S_ERR_INVALID_VALUE;
+    const SweepPlanLayout L = sweep_plan_layout(num_pieces, q_windows, heads, head_dim);
+    if (plan_bytes < L.total) return F3S_ERR_WORKSPACE;
+    if ((int64_t)num_pieces * L.groups > INT32_MAX) return F3S_ERR_TOO_LARGE;
+    std::vector<int32_t> out((size_t)num_pieces * 4);
+    std::vector<int> seen(q_windows, 0), next_block(q_windows, -1), count(q_windows, 0);
+    for (int i = 0; i < num_pieces; ++i) {
+        const int32_t* pc = pieces + 4 * (size_t)i;
+        const int w = pc[0];
+        if (w < q_window_base || w >= q_window_base + q_windows || w >= nrw) return F3S_ERR_BAD_FORMAT;
+        const int s = w - q_window_base;
+        if (count[s] == 0) next_block[s] = offsets[w];
+        if (pc[1] != next_block[s] || pc[2] < pc[1] || pc[2] > offsets[w + 1]) return F3S_ERR_BAD_FORMAT;
+        if (pc[2] == pc[1] && offsets[w + 1] != offsets[w]) return F3S_ERR_BAD_FORMAT;  // empty piece of a window with blocks
+        if (count[s] >= kSweepIndexMask) return F3S_ERR_TOO_LARGE;
+        next_block[s] = pc[2];
+        out[4 * (size_t)i + 0] = w;
+        out[4 * (size_t)i + 1] = pc[1];
+        out[4 * (size_t)i + 2] = pc[2];
+        out[4 * (size_t)i + 3] = count[s]++;
+    }
+    for (int s = 0; s < q_windows; ++s)
+        if (count[s] > 0 && next_block[s] != offsets[q_window_base + s + 1]) return F3S_ERR_BAD_FORMAT;  // not covered
+    for (int i = num_pieces - 1; i >= 0; --i) {  // the last piece of every window
+        const int s = out[4 * (size_t)i] - q_window_base;
+        if (!seen[s]) {
+            seen[s] = 1;
+            out[4 * (size_t)i + 3] |= kSweepLast;
+        }
+    }
+    PlanHeader h{};
+    h.num_pieces = h.max_pieces = num_pieces;
+    h.heads = heads;
+    h.head_dim = head_dim;
+    h.groups = L.groups;
+    h.hg = L.hg;
+    h.splits_off = (long long)L.states;  // no split records
+    h.partials_off = (long long)L.states;
+    h.states_off = (long long)L.states;
+    h.mode = kPlanSweep;
+    char* base = static_cast<char*>(plan);
+    F3S_CUDA_TRY(cudaMemcpyAsync(base, &h, sizeof(h), cudaMemcpyHostToDevice, stream));
+    if (num_pieces > 0)
+        F3S_CUDA_TRY(cudaMemcpyAsync(base + L.pieces, out.data(), out.size() * 4, cudaMemcpyHostToDevice, stream));
+    F3S_CUDA_TRY(cudaStreamSynchronize(stream));  // `out` goes away on return
+    return F3S_SUCCESS;
+}
+
 int make_plan_impl(const int* offsets, const int* order, int num_items, int64_t num_blocks, int T, int heads,
                    int head_dim, void* plan, size_t plan_bytes, cudaStream_t stream) {
     if (num_items < 0 || num_blocks < 0 || T < 1 || heads <= 0) return F3S_ERR_INVALID_VALUE;
@@ -1251,9 +1399,18 @@ int forward_impl(const void* Q, const void* K, const void* V, void* O, int o_dty
     prm.kv_col_base = range.kv_col_base;
     prm.kv_cols = (int)(((int64_t)kv_rows + 15) / 16);
     if ((int64_t)num_items * prm.groups > INT32_MAX) return F3S_ERR_TOO_LARGE;
-    // zero the abort flag and the ticket counter (adjacent words); the
-    // status word stays sticky
+    // sweep plans: the per-window, per-head piece counters follow the
+    // workspace header (f3s_sweep_workspace_size)
+    prm.seq = reinterpret_cast<int*>(static_cast<char*>(ws) + kWsHeaderBytes);
+    prm.seq_cap = (long long)((ws_bytes - kWsHeaderBytes) / sizeof(int));
+    // zero the abort flag and the ticket counter (adjacent words) and the
+    // sweep counters this launch can use; the status word stays sticky
     F3S_CUDA_TRY(cudaMemsetAsync(ws, 0, 2 * sizeof(int), stream));
+    if (plan && prm.seq_cap > 0) {
+        const long long need = (long long)prm.q_windows * heads;
+        const long long n = need < prm.seq_cap ? need : prm.seq_cap;
+        F3S_CUDA_TRY(cudaMemsetAsync(prm.seq, 0, (size_t)n * sizeof(int), stream));
+    }
     const bool m = range.merge;
     if (head_dim == 64) {
         switch (hg) {
@@ -1349,6 +1506,26 @@ int f3s_load_plan(const int32_t* h_pieces, int32_t num_pieces, const int32_t* h_
                   int32_t head_dim, void* d_plan, size_t plan_bytes, f3s_stream_t stream) {
     return f3s::load_plan_impl(h_pieces, num_pieces, h_splits, num_split, num_split_pieces, h_window_offsets,
                                num_row_windows, heads, head_dim, d_plan, plan_bytes, (cudaStream_t)stream);
+}
+
+size_t f3s_sweep_plan_size(int32_t num_pieces, int32_t q_windows, int32_t heads, int32_t head_dim) {
+    if (num_pieces < 0 || q_windows < 0 || heads <= 0) return 0;
+    if (head_dim != 64 && head_dim != 128) return 0;
+    return f3s::sweep_plan_layout(num_pieces, q_windows, heads, head_dim).total;
+}
+
+size_t f3s_sweep_workspace_size(int32_t q_rows, int32_t heads) {
+    if (q_rows < 0 || heads <= 0) return 0;
+    const size_t q_windows = ((size_t)q_rows + 15) / 16;
+    return f3s::kWsHeaderBytes + f3s::align_up(q_windows * heads * sizeof(int), 256);
+}
+
+int f3s_load_sweep_plan(const int32_t* h_pieces, int32_t num_pieces, const int32_t* h_window_offsets,
+                        int32_t num_row_windows, int32_t q_window_base, int32_t q_windows, int32_t heads,
+                        int32_t head_dim, void* d_plan, size_t plan_bytes, f3s_stream_t stream) {
+    f3s::NvtxRange nvtx_("f3s_load_sweep_plan");
+    return f3s::load_sweep_plan_impl(h_pieces, num_pieces, h_window_offsets, num_row_windows, q_window_base,
+                                     q_windows, heads, head_dim, d_plan, plan_bytes, (cudaStream_t)stream);
 }
 
 int f3s_forward(const void* d_Q, const void* d_K, const void* d_V, float* d_O, const int32_t* d_window_offsets,

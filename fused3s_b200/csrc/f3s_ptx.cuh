@@ -85,6 +85,38 @@ static __device__ __noinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t par
     }
 }
 
+// Acquire load / release store of a flag in global memory (GPU scope): the
+// reader of a flag set with st_release_gpu sees every write the setter made
+// before it.
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Waits until *flag == want (set by another CTA with st_release_gpu); bounded
+// by the global timer and the abort flag like every wait in the library.
+static __device__ __noinline__ bool flag_wait_bounded(const int* flag, int want, const ErrorSink e,
+                                                      uint64_t timeout_ns) {
+    if (ld_acquire_gpu(flag) == want) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+#pragma unroll 1
+        for (int i = 0; i < 16; ++i)
+            if (ld_acquire_gpu(flag) == want) return true;
+        if (load_volatile(e.abort)) return false;
+        if (global_timer_ns() - t0 > timeout_ns) {
+            raise_error(e, F3S_ERR_TIMEOUT);
+            return false;
+        }
+        __nanosleep(256);
+    }
+}
+
 // Short bounded wait that ignores the abort flag: used on the abort path to
 // let this CTA's own bulk copies land before it exits.
 __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity, uint64_t timeout_ns) {

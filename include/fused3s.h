@@ -248,6 +248,33 @@ int f3s_load_plan(const int32_t* h_pieces, int32_t num_pieces, const int32_t* h_
                   int32_t head_dim, void* d_plan, size_t plan_bytes, f3s_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Sweep plan (no reference counterpart): a caller-built schedule in which
+ * a window may run as several pieces that are processed one after another
+ * inside one forward launch, carrying the window's running softmax state
+ * (row max, row sum, unnormalised O) from piece to piece in the plan.  Its
+ * purpose is locality: windows cut at block-column chunk boundaries and the
+ * pieces listed chunk by chunk make every SM read one L2-sized range of K / V
+ * at a time, while no partial state per piece is kept.
+ *
+ * h_pieces: int32[4 * num_pieces] in processing order, (window, first block,
+ *   end block, unused).  The pieces of a window must appear in ascending
+ *   block order and cover its blocks [window_offsets[w], window_offsets[w+1])
+ *   exactly once; a piece holds at least one block unless its window has
+ *   none.  Windows must lie in [q_window_base, q_window_base + q_windows).
+ * Validated on the host (F3S_ERR_BAD_FORMAT); copies synchronously.
+ * A piece waits (bounded) until the previous piece of its window has stored
+ * the state: run a sweep plan with f3s_forward / f3s_forward_ex (one launch
+ * runs every piece), with a workspace of f3s_sweep_workspace_size(q_rows,
+ * heads) bytes (per-window counters, cleared by each launch).  The result
+ * equals the unsplit forward within the same tolerance.
+ * ---------------------------------------------------------------------- */
+size_t f3s_sweep_plan_size(int32_t num_pieces, int32_t q_windows, int32_t heads, int32_t head_dim);
+size_t f3s_sweep_workspace_size(int32_t q_rows, int32_t heads);
+int f3s_load_sweep_plan(const int32_t* h_pieces, int32_t num_pieces, const int32_t* h_window_offsets,
+                        int32_t num_row_windows, int32_t q_window_base, int32_t q_windows, int32_t heads,
+                        int32_t head_dim, void* d_plan, size_t plan_bytes, f3s_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Part of a plan's work, with K / V holding only some block columns (no
  * reference counterpart: the reference reads all of K / V on one device).
  *
@@ -262,7 +289,8 @@ int f3s_load_plan(const int32_t* h_pieces, int32_t num_pieces, const int32_t* h_
  * piece of the split windows has run -- over one or several calls, e.g. one
  * per K / V slice passed around a ring of GPUs -- f3s_plan_merge writes
  * their O rows.  f3s_forward_ex with a plan equals f3s_forward_pieces over
- * all pieces with the whole K / V, then f3s_plan_merge.
+ * all pieces with the whole K / V, then f3s_plan_merge.  (Not for sweep
+ * plans, whose pieces must all run in one launch.)
  * Other arguments as f3s_forward_ex (d_order is not needed).
  * ---------------------------------------------------------------------- */
 int f3s_forward_pieces(const void* d_Q, const void* d_K, const void* d_V, void* d_O, int32_t o_dtype,

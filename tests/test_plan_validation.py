@@ -65,3 +65,31 @@ def test_inconsistent_plans_are_rejected(lib):
         if name == "record slot never used":
             s = s + [(1, 5, 1, 0)]  # w1 has a record but its single empty piece has slot -1
         assert load(lib, p, s, k) == _lib.F3S_ERR_BAD_FORMAT, name
+
+
+def load_sweep(lib, pieces, q_window_base=0, q_windows=NRW):
+    p = np.ascontiguousarray(np.asarray(pieces, np.int32).reshape(-1, 4))
+    size = lib.f3s_sweep_plan_size(p.shape[0], q_windows, 1, 64)
+    fake_plan = 1 << 20
+    return lib.f3s_load_sweep_plan(p.ctypes.data, p.shape[0], OFF.ctypes.data, NRW, q_window_base, q_windows, 1,
+                                   64, fake_plan, size, None)
+
+
+def test_sweep_plans_are_validated(lib):
+    """Sweep plans (f3s_load_sweep_plan): a window's pieces in ascending block
+    order covering its blocks once, windows inside the slab."""
+    good = [(0, 0, 2, 0), (2, 5, 9, 0), (0, 2, 5, 0), (1, 5, 5, 0), (3, 9, 12, 0)]
+    assert load_sweep(lib, good) != _lib.F3S_ERR_BAD_FORMAT
+    assert load_sweep(lib, [(2, 5, 7, 0), (3, 9, 12, 0), (2, 7, 9, 0)], 2, 2) != _lib.F3S_ERR_BAD_FORMAT
+    bad = {
+        "out of column order": [(0, 2, 5, 0), (0, 0, 2, 0)],
+        "overlap": [(0, 0, 3, 0), (0, 2, 5, 0)],
+        "gap": [(0, 0, 2, 0), (0, 3, 5, 0)],
+        "not covered": [(0, 0, 2, 0)],
+        "empty piece of a window with blocks": [(0, 0, 0, 0), (0, 0, 5, 0)],
+        "window outside the slab": [(3, 9, 12, 0)],
+        "piece beyond its window": [(2, 5, 10, 0)],
+    }
+    for name, pieces in bad.items():
+        qb, qw = (0, 3) if name == "window outside the slab" else (0, NRW)
+        assert load_sweep(lib, pieces, qb, qw) == _lib.F3S_ERR_BAD_FORMAT, name
