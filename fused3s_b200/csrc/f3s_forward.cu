@@ -51,8 +51,19 @@
 
 namespace f3s {
 
+// Consumer warps per CTA (plus one producer warp): 8 -- one per head of an
+// 8-head group, or SPLITS = 8 / HG per head.  F3S_WIDE_CONSUMERS builds the
+// d = 64, 8-head variant with 16 consumer warps (two per head, alternate
+// blocks) for comparison.
 constexpr int kConsumerWarps = 8;
-constexpr int kFwdThreads = (kConsumerWarps + 1) * 32;
+template <int D, int HG>
+constexpr int consumer_warps() {
+#ifdef F3S_WIDE_CONSUMERS
+    return D == 64 && HG == 8 ? 16 : kConsumerWarps;
+#else
+    return kConsumerWarps;
+#endif
+}
 constexpr int kSmemBudget = 227 * 1024;
 constexpr uint64_t kWaitTimeoutNs = 10ull * 1000 * 1000 * 1000;  // 10 s: far above any legal wait
 constexpr float kLog2e = 1.4426950408889634f;
@@ -60,7 +71,9 @@ constexpr float kLazyLog2 = 8.0f;  // running-max slack before an O rescale (p <
 
 template <int D, int HG>
 struct FwdCfg {
-    static constexpr int SPLITS = kConsumerWarps / HG;
+    static constexpr int CW = consumer_warps<D, HG>();  // consumer warps
+    static constexpr int THREADS = (CW + 1) * 32;
+    static constexpr int SPLITS = CW / HG;
     static constexpr int HC = HG * D / 64;           // 128-byte head-chunks per node in one tile
     // A tile arrives as two TMA boxes of HA and HB head-chunks (HA odd,
     // HB = 0 or 1), node-major in shared memory: see chunk_row().
@@ -135,12 +148,12 @@ struct PlanHeader {
 };
 static_assert(sizeof(PlanHeader) == 256, "plan header is 256 bytes");
 
-// Plan modes.  kPlanPieces: a split window's pieces write partial states
-// into their own slots, merged after the kernel (k_merge_pieces).
-// kPlanSweep: a window's pieces run one after another (each waits for the
-// previous one), carrying one running state per window and head: a piece
-// loads it, folds in its own blocks and stores it back; the last writes O.
-constexpr int kPlanPieces = 0;
+// Plan modes.  0 (make_plan / load_plan): a split window's pieces write
+// partial states into their own slots, merged after the kernel
+// (k_merge_pieces).  kPlanSweep: a window's pieces run one after another
+// (each waits for the previous one), carrying one running state per window
+// and head: a piece loads it, folds in its own blocks and stores it back; the
+// last writes O.
 constexpr int kPlanSweep = 1;
 // piece info of a sweep plan: index of the piece within its window, and a
 // flag for the window's last piece
@@ -243,7 +256,7 @@ __device__ __forceinline__ uint32_t chunk_row(int hc, int n) {
 }
 
 template <int D, int HG>
-__global__ void __launch_bounds__(kFwdThreads, 1)
+__global__ void __launch_bounds__(FwdCfg<D, HG>::THREADS, 1)
     k_fused3s(const __grid_constant__ FwdMaps maps, const FwdParams p) {
     using C = FwdCfg<D, HG>;
     constexpr int S = C::STAGES;
@@ -279,7 +292,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         for (int q = 0; q < 2; ++q) {
             mbar_init(qfull(q), 1);
-            mbar_init(qempty(q), kConsumerWarps);
+            mbar_init(qempty(q), C::CW);
         }
         mbar_init(mfull, C::SPLITS > 1 ? (C::SPLITS - 1) * HG : 1);
         mbar_init(mempty, HG);
@@ -287,7 +300,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     __syncthreads();
 
-    if (warp == kConsumerWarps) {
+    if (warp == C::CW) {
         // ------------------------------------------------------ producer --
         // The whole warp runs this loop.  A block's K and V tiles are NBOX
         // boxes each, issued by the lane that claimed the block (rounds of
@@ -525,11 +538,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // Per-lane shared-memory offsets of this warp's head inside a tile, per
     // 16-wide k-step: ldmatrix rows of K (B operand of Q K^T) and of V (B
     // operand of P V, transposed), computed once.
-    uint32_t offk[KS], offv[KS];
+    // (The wide variant, with fewer registers per thread, recomputes them.)
+    constexpr bool HOIST = C::CW == kConsumerWarps;
+    uint32_t offk[HOIST ? KS : 1], offv[HOIST ? KS : 1];
+    auto koff = [&](int ks) -> uint32_t {
+        return swz128(chunk_row<C::HA>(hh * (D / 64) + ks / 4, b_row), (ks & 3) * 2 + b_chk);
+    };
+    auto voff = [&](int ks) -> uint32_t {
+        return swz128(chunk_row<C::HA>(hh * (D / 64) + ks / 4, a_row), (ks & 3) * 2 + a_chk);
+    };
+    if constexpr (HOIST) {
 #pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {
-        offk[ks] = swz128(chunk_row<C::HA>(hh * (D / 64) + ks / 4, b_row), (ks & 3) * 2 + b_chk);
-        offv[ks] = swz128(chunk_row<C::HA>(hh * (D / 64) + ks / 4, a_row), (ks & 3) * 2 + a_chk);
+        for (int ks = 0; ks < KS; ++ks) {
+            offk[ks] = koff(ks);
+            offv[ks] = voff(ks);
+        }
     }
     // position of this split's next block in its sub-ring (slot l % S_SUB
     // and phase parity (l / S_SUB) & 1 of its l-th block over all windows)
@@ -569,7 +592,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks) {
                 uint32_t k0, k1, k2, k3;
-                ldsm_x4(kt + offk[ks], k0, k1, k2, k3);
+                uint32_t ko;
+                if constexpr (HOIST) ko = offk[ks]; else ko = koff(ks);
+                ldsm_x4(kt + ko, k0, k1, k2, k3);
                 if (ks == 0) {
                     mma_16816_zero(sc[0], qa[ks], k0, k1);
                     mma_16816_zero(sc[1], qa[ks], k2, k3);
@@ -592,7 +617,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
             for (int jj = 0; jj < KS; ++jj) {
                 uint32_t v0, v1, v2, v3;
-                ldsm_x4_t(vt + offv[jj], v0, v1, v2, v3);
+                uint32_t vo;
+                if constexpr (HOIST) vo = offv[jj]; else vo = voff(jj);
+                ldsm_x4_t(vt + vo, v0, v1, v2, v3);
                 mma_16816(o[2 * jj], pa, v0, v1);
                 mma_16816(o[2 * jj + 1], pa, v2, v3);
             }
@@ -1078,7 +1105,7 @@ static int launch_variant(const void* Q, const void* K, const void* V, FwdParams
     const int ctas = forward_grid_limit();
     const int items = prm.num_items * prm.groups;
     const int grid = prm.plan ? ctas : std::max(1, std::min(items, ctas));
-    k_fused3s<D, HG><<<grid, kFwdThreads, C::SMEM, stream>>>(maps, prm);
+    k_fused3s<D, HG><<<grid, C::THREADS, C::SMEM, stream>>>(maps, prm);
     F3S_LAUNCH_CHECK();
     if (prm.plan && merge) {
         k_merge_pieces<D><<<2 * sms, 256, 0, stream>>>(prm.plan, prm.O, prm.heads, prm.num_nodes, prm.q_window_base,
