@@ -681,6 +681,11 @@ def run_ours(args):
     compulsory = ((r1 - r0) * H * d * 2 + 2 * N * H * d * 2 + (r1 - r0) * H * d * O.element_size()
                   + 4 * my_blocks + 4 * (nrw + 1) + (my_blocks if hints is not None else 0))
     hbm_peak, tc_peak, peak_kind = measured_peaks()
+    # the peak of the tensor instruction the kernel issues (mma.sync), measured
+    # here on this GPU: 16 warps per SM, 8 independent chains each
+    mma_tflops = _lib.ctypes.c_double(0.0)
+    st = lib.f3s_probe_mma_sync(16, 4096, mma_tflops, stream.cuda_stream)
+    mma_peak = mma_tflops.value if st == 0 else None
     achieved = bytes_launch / (kernel_ms / 1e3) / 1e9
     traffic = ncu_traffic(args.config, H, d, args.split) if (world == 1 and args.graph_seed is None
                                                              and args.l2_hints == "on" and args.l2_keep == 0.5
@@ -697,7 +702,9 @@ def run_ours(args):
                         "fused kernel's own event time; L2 hits let it exceed the copy bandwidth. dram_frac: "
                         "ncu DRAM bytes of the same full-size launch over the same time.",
                 "tensor_tflops": flops_launch / (kernel_ms / 1e3) / 1e12, "tensor_peak": tc_peak,
-                "tensor_frac": flops_launch / (kernel_ms / 1e3) / 1e12 / tc_peak}
+                "tensor_frac": flops_launch / (kernel_ms / 1e3) / 1e12 / tc_peak,
+                "mma_sync_peak_tflops": mma_peak,
+                "mma_sync_frac": (flops_launch / (kernel_ms / 1e3) / 1e12 / mma_peak) if mma_peak else None}
         if traffic is not None:
             roof["dram_gbs"] = traffic / (kernel_ms / 1e3) / 1e9
             roof["dram_frac"] = roof["dram_gbs"] / hbm_peak

@@ -73,6 +73,7 @@ SIGNATURES = {
     "f3s_1tb1rw_launch": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _P]),
     "f3s_half_from_float": (ctypes.c_int, [_P, _P, _I64, _P]),
     "f3s_selftest_wait_timeout": (ctypes.c_int, [_U64, _P, _SZ, _P]),
+    "f3s_probe_mma_sync": (ctypes.c_int, [_I32, _I32, ctypes.POINTER(ctypes.c_double), _P]),
 }
 
 _lib = None

@@ -21,7 +21,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 LIB = PKG / "libfused3s.so"
-SOURCES = ["f3s_api.cu", "f3s_format.cu", "f3s_forward.cu", "f3s_peer.cu", "f3s_text.cu"]
+SOURCES = ["f3s_api.cu", "f3s_format.cu", "f3s_forward.cu", "f3s_peer.cu", "f3s_probe.cu", "f3s_text.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -348,6 +348,16 @@ int f3s_1tb1rw_launch(const void* Q, const void* K, const void* V, float* O_out,
 int f3s_half_from_float(const float* d_in, void* d_out, int64_t n, f3s_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Throughput of mma.sync.m16n8k16 (f16 x f16 -> f32), the tensor-core
+ * instruction of the fused kernel, on the current device: one CTA of
+ * warps_per_sm warps per SM, each warp running 8 independent accumulator
+ * chains for iters iterations; writes TFLOP/s to *h_tflops (synchronises
+ * `stream`).  The tensor-side roofline denominator of the fused kernel (no
+ * reference counterpart).
+ * ---------------------------------------------------------------------- */
+int f3s_probe_mma_sync(int32_t warps_per_sm, int32_t iters, double* h_tflops, f3s_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Self-test of the failure path: launches a kernel that waits on an
  * mbarrier nobody arrives on, with the given bound.  The wait gives up,
  * records F3S_ERR_TIMEOUT in the workspace and the kernel returns normally;
