@@ -629,20 +629,19 @@ __global__ void __launch_bounds__(FwdCfg<D, HG>::THREADS, 1)
         // blocks in the sub-ring, in order): their QK^T, exp and P.V chains
         // interleave, and one max update / rescale covers 16 * NB columns.
         constexpr int NB = C::NB;
-        constexpr int STEP = NB * C::SPLITS;
         struct Step {
             float sc[NB][2][4];
             uint32_t st[NB];
             int n;  // blocks in the step (0: past the window's end)
         };
-        // Waits for the step's stages and issues its QK^T.
-        auto fetch = [&](Step& S, int j) -> bool {
+        // Waits for the step's stages (at most nmax blocks) and issues its QK^T.
+        auto fetch = [&](Step& S, int j, int nmax) -> bool {
             if (j >= nb) {
                 S.n = 0;
                 return true;
             }
             const int left = (nb - 1 - j) / C::SPLITS + 1;  // this split's blocks from j on
-            S.n = left < NB ? left : NB;                     // warp-uniform
+            S.n = left < nmax ? left : nmax;                 // warp-uniform
             uint32_t ph[NB];
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
@@ -724,8 +723,8 @@ __global__ void __launch_bounds__(FwdCfg<D, HG>::THREADS, 1)
             }
         };
         Step A;
-        for (int j = sp; j < nb; j += STEP) {
-            if (!(ok = fetch(A, j))) break;
+        for (int j = sp; j < nb; j += NB * C::SPLITS) {
+            if (!(ok = fetch(A, j, NB))) break;
             process(A);
         }
         if (!ok) return;
