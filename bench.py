@@ -92,14 +92,14 @@ def lib_is_default() -> bool:
     return Path(_lib.LIB_PATH).resolve() == (ROOT / "fused3s_b200" / "libfused3s.so").resolve()
 
 
-def ncu_traffic(config: str, heads: int, dim: int, split: str):
+def ncu_traffic(config: str, heads: int, dim: int, split: str, order: str, hints: str):
     """DRAM bytes (read + write) per fused-kernel launch of this exact
     workload, from the committed ncu summary (a one-pass capture of the
     full-size launch), or None."""
-    p = ROOT / "profiles" / "fused3s_dram_traffic.md"
+    p = ROOT / "profiles" / "k_fused3s_dram_traffic.md"
     if not p.exists():
         return None
-    key = re.escape(f"dram_bytes_per_launch[{config},H{heads},d{dim},{split}]")
+    key = re.escape(f"dram_bytes_per_launch[{config},H{heads},d{dim},{split},{order},hints-{hints}]")
     m = re.search(key + r":\s*([0-9.eE+]+)", p.read_text())
     return float(m.group(1)) if m else None
 
@@ -687,9 +687,9 @@ def run_ours(args):
     st = lib.f3s_probe_mma_sync(16, 4096, mma_tflops, stream.cuda_stream)
     mma_peak = mma_tflops.value if st == 0 else None
     achieved = bytes_launch / (kernel_ms / 1e3) / 1e9
-    traffic = ncu_traffic(args.config, H, d, args.split) if (world == 1 and args.graph_seed is None
-                                                             and args.l2_hints == "on" and args.l2_keep == 0.5
-                                                             and lib_is_default()) else None
+    traffic = ncu_traffic(args.config, H, d, args.split, args.order, args.l2_hints) if (
+        world == 1 and args.graph_seed is None and args.l2_keep == 0.5 and args.seed == 42 and lib_is_default()) \
+        else None
 
     result = None
     if rank == 0:

@@ -43,6 +43,7 @@
 //     status word in the workspace instead of hanging.
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 #include <vector>
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -634,27 +635,29 @@ __global__ void __launch_bounds__(FwdCfg<D, HG>::THREADS, 1)
             uint32_t st[NB];
             int n;  // blocks in the step (0: past the window's end)
         };
-        // Waits for the step's stages (at most nmax blocks) and issues its QK^T.
-        auto fetch = [&](Step& S, int j, int nmax) -> bool {
-            if (j >= nb) {
-                S.n = 0;
-                return true;
+        // Waits for the step's stages and issues its QK^T: all NB blocks when
+        // `whole` is std::true_type (the common case, without per-block
+        // tests), else the split's remaining blocks of the window (< NB).
+        auto fetch = [&](Step& S, int j, auto whole) -> bool {
+            constexpr bool FULL = decltype(whole)::value;
+            if constexpr (FULL) {
+                S.n = NB;
+            } else {
+                S.n = (nb - 1 - j) / C::SPLITS + 1;  // this split's blocks from j on, warp-uniform
             }
-            const int left = (nb - 1 - j) / C::SPLITS + 1;  // this split's blocks from j on
-            S.n = left < nmax ? left : nmax;                 // warp-uniform
             uint32_t ph[NB];
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
                 S.st[b] = sp * C::S_SUB + ring_pos;
                 ph[b] = ring_par;
-                if (b < S.n && ++ring_pos == (uint32_t)C::S_SUB) {
+                if ((FULL || b < S.n) && ++ring_pos == (uint32_t)C::S_SUB) {
                     ring_pos = 0;
                     ring_par ^= 1u;
                 }
             }
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
-                if (b < S.n) {
+                if (FULL || b < S.n) {
                     if (!wait_fast(full(S.st[b]), ph[b], err, p.timeout_ns)) return false;
                     qk_tile(kv_s + S.st[b] * 2 * C::TILE, S.sc[b]);
                     if (p.tail != 0) mask_tail(S.sc[b], stage_col[S.st[b]]);
@@ -666,7 +669,8 @@ __global__ void __launch_bounds__(FwdCfg<D, HG>::THREADS, 1)
             return true;
         };
         // Softmax update and P.V of a fetched step; frees its stages.
-        auto process = [&](Step& S) {
+        auto process = [&](Step& S, auto whole) {
+            constexpr bool FULL = decltype(whole)::value;
             float mx0 = fmaxf(fmaxf(S.sc[0][0][0], S.sc[0][0][1]), fmaxf(S.sc[0][1][0], S.sc[0][1][1]));
             float mx1 = fmaxf(fmaxf(S.sc[0][0][2], S.sc[0][0][3]), fmaxf(S.sc[0][1][2], S.sc[0][1][3]));
 #pragma unroll
@@ -674,12 +678,18 @@ __global__ void __launch_bounds__(FwdCfg<D, HG>::THREADS, 1)
                 mx0 = fmaxf(mx0, fmaxf(fmaxf(S.sc[b][0][0], S.sc[b][0][1]), fmaxf(S.sc[b][1][0], S.sc[b][1][1])));
                 mx1 = fmaxf(mx1, fmaxf(fmaxf(S.sc[b][0][2], S.sc[b][0][3]), fmaxf(S.sc[b][1][2], S.sc[b][1][3])));
             }
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2)) * kLog2e;
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2)) * kLog2e;
-            const bool up0 = mx0 > m0 + kLazyLog2, up1 = mx1 > m1 + kLazyLog2;
-            if (__any_sync(0xffffffffu, up0 || up1)) {
+            // A row's max exceeds its running max by more than kLazyLog2 iff
+            // one of the row's four lanes holds such a value (scaling by
+            // log2e is monotonic), so the vote needs no row reduction: the
+            // shuffles run only on the rare update, which then applies the
+            // row-max rule exactly as before.
+            const bool up_lane = mx0 * kLog2e > m0 + kLazyLog2 || mx1 * kLog2e > m1 + kLazyLog2;
+            if (__any_sync(0xffffffffu, up_lane)) {
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2)) * kLog2e;
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2)) * kLog2e;
+                const bool up0 = mx0 > m0 + kLazyLog2, up1 = mx1 > m1 + kLazyLog2;
                 const float mn0 = up0 ? mx0 : m0, mn1 = up1 ? mx1 : m1;
                 const float c0 = fast_exp2(m0 - mn0), c1 = fast_exp2(m1 - mn1);
                 l0 *= c0;
@@ -696,7 +706,7 @@ __global__ void __launch_bounds__(FwdCfg<D, HG>::THREADS, 1)
             }
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
-                if (b < S.n) {
+                if (FULL || b < S.n) {
                     float pr[2][4];
 #pragma unroll
                     for (int nt = 0; nt < 2; ++nt) {
@@ -719,13 +729,18 @@ __global__ void __launch_bounds__(FwdCfg<D, HG>::THREADS, 1)
             if (lane == 0) {
 #pragma unroll
                 for (int b = 0; b < NB; ++b)
-                    if (b < S.n) mbar_arrive(empty(S.st[b]));
+                    if (FULL || b < S.n) mbar_arrive(empty(S.st[b]));
             }
         };
         Step A;
         for (int j = sp; j < nb; j += NB * C::SPLITS) {
-            if (!(ok = fetch(A, j, NB))) break;
-            process(A);
+            if ((nb - 1 - j) / C::SPLITS + 1 >= NB) {
+                if (!(ok = fetch(A, j, std::true_type{}))) break;
+                process(A, std::true_type{});
+            } else {
+                if (!(ok = fetch(A, j, std::false_type{}))) break;
+                process(A, std::false_type{});
+            }
         }
         if (!ok) return;
         l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
