@@ -808,7 +808,12 @@ __global__ void __launch_bounds__(FwdCfg<D, HG>::THREADS, 1)
                 okw = __shfl_sync(0xffffffffu, okw, 0);
                 if (!okw) return;
                 __syncwarp();
-                const float4 ml = __ldcs(st4 + NT * 32 + lane);  // (m0, l0, m1, l1) of the pieces before
+                // The stored state is read from L2 (ld.global.cg), never from
+                // this SM's L1: an earlier piece of the window may have run
+                // here and left the previous contents of these lines in L1,
+                // and weak loads after lane 0's acquire were measured to hit
+                // them (sweeps that differed from run to run).
+                const float4 ml = __ldcg(st4 + NT * 32 + lane);  // (m0, l0, m1, l1) of the pieces before
                 const float M0 = fmaxf(m0, ml.x), M1 = fmaxf(m1, ml.z);
                 const float a0 = fast_exp2(ml.x - M0), b0s = fast_exp2(m0 - M0);
                 const float a1 = fast_exp2(ml.z - M1), b1s = fast_exp2(m1 - M1);
@@ -818,7 +823,7 @@ __global__ void __launch_bounds__(FwdCfg<D, HG>::THREADS, 1)
                 m1 = M1;
 #pragma unroll
                 for (int jn = 0; jn < NT; ++jn) {
-                    const float4 v = __ldcs(st4 + jn * 32 + lane);
+                    const float4 v = __ldcg(st4 + jn * 32 + lane);
                     o[jn][0] = v.x * a0 + o[jn][0] * b0s;
                     o[jn][1] = v.y * a0 + o[jn][1] * b0s;
                     o[jn][2] = v.z * a1 + o[jn][2] * b1s;
