@@ -803,17 +803,14 @@ __global__ void __launch_bounds__(FwdCfg<D, HG>::THREADS, 1)
             float4* st4 = reinterpret_cast<float4*>(reinterpret_cast<char*>(p.plan) + p.plan->states_off) +
                           fidx * (SE / 4) * 32;
             if (kpiece > 0) {
-                int okw = 1;
-                if (lane == 0) okw = flag_wait_bounded(flag, kpiece, err, p.timeout_ns) ? 1 : 0;
-                okw = __shfl_sync(0xffffffffu, okw, 0);
-                if (!okw) return;
-                __syncwarp();
-                // The stored state is read from L2 (ld.global.cg), never from
-                // this SM's L1: an earlier piece of the window may have run
-                // here and left the previous contents of these lines in L1,
-                // and weak loads after lane 0's acquire were measured to hit
-                // them (sweeps that differed from run to run).
-                const float4 ml = __ldcg(st4 + NT * 32 + lane);  // (m0, l0, m1, l1) of the pieces before
+                // Every lane waits on the flag with its own acquire load (one
+                // transaction per poll for the warp) and reads the stored
+                // state with strong GPU-scope loads.  With one lane acquiring
+                // and the others reading with weak loads, a piece sometimes
+                // folded in an older state (an earlier piece of the window
+                // ran on this SM): sweeps differed from launch to launch.
+                if (!__all_sync(0xffffffffu, flag_wait_bounded(flag, kpiece, err, p.timeout_ns))) return;
+                const float4 ml = ld_relaxed_gpu_f4(st4 + NT * 32 + lane);  // (m0, l0, m1, l1) of the pieces before
                 const float M0 = fmaxf(m0, ml.x), M1 = fmaxf(m1, ml.z);
                 const float a0 = fast_exp2(ml.x - M0), b0s = fast_exp2(m0 - M0);
                 const float a1 = fast_exp2(ml.z - M1), b1s = fast_exp2(m1 - M1);
@@ -823,7 +820,7 @@ __global__ void __launch_bounds__(FwdCfg<D, HG>::THREADS, 1)
                 m1 = M1;
 #pragma unroll
                 for (int jn = 0; jn < NT; ++jn) {
-                    const float4 v = __ldcg(st4 + jn * 32 + lane);
+                    const float4 v = ld_relaxed_gpu_f4(st4 + jn * 32 + lane);
                     o[jn][0] = v.x * a0 + o[jn][0] * b0s;
                     o[jn][1] = v.y * a0 + o[jn][1] * b0s;
                     o[jn][2] = v.z * a1 + o[jn][2] * b1s;
@@ -835,11 +832,9 @@ __global__ void __launch_bounds__(FwdCfg<D, HG>::THREADS, 1)
                 for (int jn = 0; jn < NT; ++jn)
                     __stcs(st4 + jn * 32 + lane, make_float4(o[jn][0], o[jn][1], o[jn][2], o[jn][3]));
                 __stcs(st4 + NT * 32 + lane, make_float4(m0, l0, m1, l1));
+                __threadfence();  // every lane: its state stores before the release below
                 __syncwarp();
-                if (lane == 0) {
-                    __threadfence();
-                    st_release_gpu(flag, kpiece + 1);
-                }
+                if (lane == 0) st_release_gpu(flag, kpiece + 1);
                 continue;
             }
         } else if (pslot >= 0) {

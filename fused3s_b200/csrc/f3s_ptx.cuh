@@ -94,6 +94,17 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
     return v;
 }
 
+// Strong (relaxed, GPU scope) 16-byte load: coherent at GPU scope, never
+// served from a stale copy in this SM's L1.
+__device__ __forceinline__ float4 ld_relaxed_gpu_f4(const float4* p) {
+    float4 v;
+    asm volatile("ld.relaxed.gpu.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+
 __device__ __forceinline__ void st_release_gpu(int* p, int v) {
     asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
