@@ -175,7 +175,7 @@ def workload(args):
 def build_graph(args, device):
     from fused3s_b200 import graphs as G
     t0 = time.time()
-    dev = str(device) if (device is not None and args.config in ("c4", "c5", "c4s")) else "cpu"
+    dev = str(device) if (device is not None and args.config in ("c4", "c5", "c4s", "c5s", "c5m")) else "cpu"
     g = G.make_graph(args.config, device=dev, seed=args.graph_seed)
     log(f"[bench] graph {args.config}: N={g.num_nodes} E={g.num_edges} ({time.time() - t0:.1f}s)")
     return g
@@ -756,7 +756,7 @@ def main(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c5", choices=["c1", "c2", "c3", "c4", "c5", "c4s"])
+    ap.add_argument("--config", default="c5", choices=["c1", "c2", "c3", "c4", "c5", "c4s", "c5s", "c5m"])
     ap.add_argument("--heads", type=int, default=None, help="heads (default: the configuration's)")
     ap.add_argument("--dim", type=int, default=None, choices=[64, 128], help="head dim (default: the configuration's)")
     ap.add_argument("--seed", type=int, default=42, help="seed of the Q / K / V draws")

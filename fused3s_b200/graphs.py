@@ -62,6 +62,10 @@ CONFIGS = {
     # C4's family at 2^18 nodes: K+V still exceed L2 (512 MB) while the whole
     # case holds ~2 GB on the device -- the size used for ncu captures
     "c4s": Config("c4s", 8, 64, "normal", "R-MAT N=2^18 avg deg 16 symmetrised permuted, H=8 d=64"),
+    # C5's family at 2^20 and 2^22 nodes (K+V 2.1 GB and 8.6 GB): the cases
+    # whose DRAM traffic per block stands in for C5's in ncu captures
+    "c5s": Config("c5s", 4, 128, "normal", "R-MAT N=2^20 avg deg 32 symmetrised permuted, H=4 d=128"),
+    "c5m": Config("c5m", 4, 128, "normal", "R-MAT N=2^22 avg deg 32 symmetrised permuted, H=4 d=128"),
 }
 
 
@@ -304,6 +308,10 @@ def make_graph(config: str, device: str = "cpu", seed: Optional[int] = None) -> 
         return rmat_graph(24, 32, device=device, name="c5", **kw)
     if config == "c4s":
         return rmat_graph(18, 16, device=device, name="c4s", **kw)
+    if config == "c5s":
+        return rmat_graph(20, 32, device=device, name="c5s", **kw)
+    if config == "c5m":
+        return rmat_graph(22, 32, device=device, name="c5m", **kw)
     raise ValueError(f"unknown config {config!r}")
 
 
