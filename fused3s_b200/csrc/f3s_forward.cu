@@ -120,7 +120,8 @@ struct FwdCfg {
     static constexpr int NBARS = 2 * STAGES + 6;
     static constexpr int META_OFF = BAR_OFF + NBARS * 8;
     static constexpr int WINFO_OFF = (META_OFF + STAGES * 4 + 15) / 16 * 16;
-    static constexpr int SMEM = WINFO_OFF + 4 * 16 + 1024;  // + slack to align the base to 1 KB
+    static constexpr int SINK_OFF = WINFO_OFF + 4 * 16;  // one word per consumer warp, written, never read
+    static constexpr int SMEM = SINK_OFF + CW * 4 + 1024;  // + slack to align the base to 1 KB
     static_assert(STAGES >= 2, "need at least two K/V stages");
     static_assert(SMEM <= kSmemBudget, "shared memory budget");
     static_assert(D % 64 == 0, "head_dim must be a multiple of 64");
@@ -271,6 +272,7 @@ __global__ void __launch_bounds__(FwdCfg<D, HG>::THREADS, 1)
     const uint32_t bar0 = sbase + C::BAR_OFF;
     int* stage_col = reinterpret_cast<int*>(sp8 + C::META_OFF);
     int4* winfo = reinterpret_cast<int4*>(sp8 + C::WINFO_OFF);
+    const uint32_t sink_s = sbase + C::SINK_OFF;
     auto full = [&](uint32_t s) { return bar0 + 8u * s; };
     auto empty = [&](uint32_t s) { return bar0 + 8u * (S + s); };
     auto qfull = [&](uint32_t q) { return bar0 + 8u * (2 * S + q); };
@@ -568,6 +570,7 @@ __global__ void __launch_bounds__(FwdCfg<D, HG>::THREADS, 1)
         if (wi.x < 0) return;
         const int w = wi.x, g = wi.y, nb = wi.w - wi.z;
         uint32_t qa[KS][4];
+        uint32_t qdep = 0;
         if (nb > 0) {
             const uint32_t qt = q_s + q * C::TILE;
 #pragma unroll
@@ -575,9 +578,17 @@ __global__ void __launch_bounds__(FwdCfg<D, HG>::THREADS, 1)
                 const uint32_t row = chunk_row<C::HA>(hh * (D / 64) + ks / 4, a_row);
                 ldsm_x4(qt + swz128(row, (ks & 3) * 2 + a_chk), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
             }
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) qdep ^= qa[ks][0] ^ qa[ks][1] ^ qa[ks][2] ^ qa[ks][3];
         }
+        // Free the Q slot only once the fragments are in registers: the
+        // arrive follows a store of a value computed from them.  An arrive issued right
+        // after the ldmatrix instructions let the producer's next Q copy into
+        // this slot race with them (rows of a warp's Q were seen to change in
+        // sweep plans, where a warp that waited on its flag is the last to
+        // arrive and the producer is already waiting).
         __syncwarp();
-        if (lane == 0) mbar_arrive(qempty(q));
+        if (lane == 0) mbar_arrive_after(qempty(q), sink_s + 4u * (uint32_t)warp, qdep);
 
         float o[NT][4];
 #pragma unroll

@@ -48,6 +48,18 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// Arrive once `dep` is available: `dep` is first stored to a scratch word in
+// shared memory, and a store cannot issue before the instructions that
+// produced its value (e.g. ldmatrix loads from the buffer this arrive frees)
+// have written their registers.
+__device__ __forceinline__ void mbar_arrive_after(uint32_t bar, uint32_t sink, uint32_t dep) {
+    asm volatile(
+        "st.shared.b32 [%1], %2;\n\t"
+        "mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar),
+        "r"(sink), "r"(dep)
+        : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                  : "memory");
