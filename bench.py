@@ -697,12 +697,14 @@ def run_ours(args):
     if rank == 0:
         clocks = clk.summary()
         roof = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                "frac": achieved / hbm_peak, "traffic": traffic, "peak_kind": peak_kind,
+                "frac": achieved / hbm_peak, "alg_frac": achieved / hbm_peak, "traffic": traffic,
+                "peak_kind": peak_kind,
                 "alg_bytes_per_launch": bytes_launch, "compulsory_bytes": compulsory,
                 "kernel_ms": kernel_ms, "merge_ms": merge_ms,
-                "note": "achieved/frac: algorithmic bytes (every block's K and V tiles, Q and O tiles) over the "
-                        "fused kernel's own event time; L2 hits let it exceed the copy bandwidth. dram_frac: "
-                        "ncu DRAM bytes of the same full-size launch over the same time.",
+                "note": "achieved/frac (= alg_frac): algorithmic bytes (every block's K and V tiles, Q and O "
+                        "tiles) over the fused kernel's own event time, not DRAM bytes; L2 hits let it exceed the "
+                        "copy bandwidth. dram_frac: ncu DRAM bytes of the same launch (one-pass capture, "
+                        "profiles/k_fused3s_dram_traffic.md) over the same time; absent where not captured.",
                 "tensor_tflops": flops_launch / (kernel_ms / 1e3) / 1e12, "tensor_peak": tc_peak,
                 "tensor_frac": flops_launch / (kernel_ms / 1e3) / 1e12 / tc_peak,
                 "mma_sync_peak_tflops": mma_peak,
