@@ -816,10 +816,8 @@ __global__ void __launch_bounds__(FwdCfg<D, HG>::THREADS, 1)
             if (kpiece > 0) {
                 // Every lane waits on the flag with its own acquire load (one
                 // transaction per poll for the warp) and reads the stored
-                // state with strong GPU-scope loads.  With one lane acquiring
-                // and the others reading with weak loads, a piece sometimes
-                // folded in an older state (an earlier piece of the window
-                // ran on this SM): sweeps differed from launch to launch.
+                // state with strong GPU-scope loads, so each lane's reads are
+                // ordered after its own acquire, whatever the cache holds.
                 if (!__all_sync(0xffffffffu, flag_wait_bounded(flag, kpiece, err, p.timeout_ns))) return;
                 const float4 ml = ld_relaxed_gpu_f4(st4 + NT * 32 + lane);  // (m0, l0, m1, l1) of the pieces before
                 const float M0 = fmaxf(m0, ml.x), M1 = fmaxf(m1, ml.z);
