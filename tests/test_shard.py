@@ -161,3 +161,25 @@ def test_device_er_generator_family():
     sizes = np.bincount(lab)
     assert sizes.max() <= 500  # components stay inside one graph of at most 500 nodes
     assert np.all(np.abs(rows - ci) < 500)  # graphs are laid out one after another
+
+
+def test_kv_share_rows_cover_k_and_v():
+    """Each rank's share of K / V rows for the host-memory forward
+    (hostio.kv_share_rows): whole block columns, equal padded sizes (what
+    the all-gather into the replica needs), in rank order, together exactly
+    the N rows, empty shares for surplus ranks."""
+    from fused3s_b200 import hostio
+
+    for n in (1, 15, 16, 17, 1000, 2708, 1 << 20):
+        for world in (1, 2, 3, 4, 8):
+            share, rows = hostio.kv_share_rows(n, world)
+            assert share % 16 == 0 and world * share >= n
+            assert len(rows) == world
+            assert rows[0][0] == 0 and rows[-1][1] == n
+            for (a, b), (c, d) in zip(rows[:-1], rows[1:]):
+                assert b == c
+            for r, (a, b) in enumerate(rows):
+                assert a == min(r * share, n) and b - a <= share
+                assert a % 16 == 0 or a == n
+    share, rows = hostio.kv_share_rows(17, 8)  # two block columns over eight ranks
+    assert share == 16 and rows[:2] == [(0, 16), (16, 17)] and all(a == b for a, b in rows[2:])
