@@ -257,8 +257,9 @@ def generate_balanced_window_order(fmt: BlockSparseFormat) -> torch.Tensor:
 def locality_order(fmt: BlockSparseFormat, heavy_blocks: int, order: Optional[torch.Tensor] = None) -> torch.Tensor:
     """A work order for the fused forward that keeps neighbouring windows
     together: the windows with more than `heavy_blocks` blocks first, heaviest
-    first (they bound the tail, as in the balanced order), then every other
-    window in ascending id.  Neighbouring windows of a graph whose nodes are
+    first (they bound the tail, as in the balanced order; equal counts keep
+    their order in `order`, ascending id for the default and for the
+    balanced order), then every other window in ascending id.  Neighbouring windows of a graph whose nodes are
     numbered by locality (communities, block-diagonal batches) share block
     columns, so they then run at the same time and their K / V tiles are
     reused from L2; the result is the same as for any other order (windows
@@ -273,7 +274,7 @@ def locality_order(fmt: BlockSparseFormat, heavy_blocks: int, order: Optional[to
     cnt = (off[wins + 1] - off[wins]).to(torch.int64)
     heavy = cnt > heavy_blocks
     hw, hc = wins[heavy], cnt[heavy]
-    # heaviest first; ties by ascending id (a stable sort of the ids by -count)
+    # heaviest first; ties keep their listed order (a stable sort by -count)
     idx = torch.sort(-hc, stable=True).indices if hw.numel() else hc
     light = torch.sort(wins[~heavy]).values
     return torch.cat([hw[idx], light]).to(torch.int32).contiguous()

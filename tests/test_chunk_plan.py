@@ -114,3 +114,29 @@ def test_explicit_cuts_equal_multiples_and_cover_uneven_slices():
     assert blocks == list(range(off[-1]))
     with pytest.raises(ValueError):
         column_chunk_pieces(off, cols, order, col_cuts=np.array([0, nrw // 2]))  # does not cover
+
+
+def test_locality_order_is_a_permutation_heavy_first():
+    """api.locality_order on CPU tensors: a permutation of the listed
+    windows; windows above the threshold first, heaviest first with ties in
+    their listed order; then every other window in ascending id."""
+    import types
+
+    import torch
+
+    from fused3s_b200 import api
+
+    rng = np.random.default_rng(3)
+    cnt = rng.integers(0, 40, 500)
+    cnt[[7, 90, 91, 300]] = 200  # ties among heavy windows
+    off = torch.from_numpy(np.concatenate([[0], np.cumsum(cnt)]).astype(np.int32))
+    fmt = types.SimpleNamespace(window_offsets=off, num_row_windows=500)
+    for subset in (None, torch.from_numpy(rng.permutation(500)[:300].astype(np.int32))):
+        got = api.locality_order(fmt, 30, order=subset).numpy()
+        wins = np.arange(500) if subset is None else subset.numpy()
+        assert sorted(got.tolist()) == sorted(wins.tolist())
+        heavy = [w for w in wins if cnt[w] > 30]
+        pos = {int(w): i for i, w in enumerate(wins)}
+        want_heavy = sorted(heavy, key=lambda w: (-cnt[w], pos[int(w)]))
+        want_light = sorted(w for w in wins if cnt[w] <= 30)
+        assert got.tolist() == [int(w) for w in want_heavy + want_light]
